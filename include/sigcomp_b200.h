@@ -1,0 +1,140 @@
+/*
+ * sigcomp_b200 - C ABI of the B200 neural codec for SigComp.
+ *
+ * These entry points replace the device half of SigComp's codec object, the
+ * object `_load_model` returns for `--device cuda` (sigcomp/main.py:189-225):
+ *   - GPUCompression.compress_chunks   (sigcomp/quant_mlp_export.py:271-323)
+ *   - GPUCompression.decompress_chunks (sigcomp/quant_mlp_export.py:325-377)
+ * with the byte-exact semantics of the reference CPU codec
+ * (sigcomp/cpu_compression.py:178-332, sigcomp/cpu_entropy_coding.py).
+ *
+ * Conventions
+ *   - Plain pointers and sizes; no framework types.  "host" entry points take
+ *     host memory (pageable or pinned) and do the copies; "_device" entry points
+ *     take device pointers already resident on the model's GPU.
+ *   - `stream` is a cudaStream_t passed as void*; NULL selects the default stream.
+ *     Every entry point returns after its work on `stream` has completed.
+ *   - Return value: SC_OK or an SC_ERR_* code; sc_last_error() gives the message
+ *     (thread-local, valid until the next call on the same thread).
+ *   - A chunk is at most `chunk_len` tokens (uint8, the SigComp "small" symbols).
+ *     A chunk's stream is a sequence of little-endian uint32 words.
+ *   - One model handle may be used by one host thread at a time.
+ */
+#ifndef SIGCOMP_B200_H
+#define SIGCOMP_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SC_API __attribute__((visibility("default")))
+#else
+#define SC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SC_OK                   0
+#define SC_ERR_INVALID_ARGUMENT 1  /* reference: ValueError (bad tokens, lengths, frames) */
+#define SC_ERR_CAPACITY         2  /* reference: OverflowError (coder output capacity) */
+#define SC_ERR_CORRUPT_STREAM   3  /* reference: ValueError("invalid range stream or mismatching entropy model") */
+#define SC_ERR_CUDA             4  /* CUDA runtime failure */
+#define SC_ERR_UNSUPPORTED      5  /* model geometry or device not supported */
+#define SC_ERR_OUT_OF_MEMORY    6
+
+typedef struct sc_model sc_model;
+
+/* Library version string. */
+SC_API const char *sc_version(void);
+
+/* Message of the last failure on this thread ("" if none). */
+SC_API const char *sc_last_error(void);
+
+/* Number of kernels this library has launched in this process (all models). */
+SC_API int64_t sc_kernel_launches(void);
+
+/*
+ * Upload an integer entropy model to `device` and return a handle.
+ * Replaces the device model built by QuantMLPCompression.__init__
+ * (sigcomp/quant_mlp_export.py:215-269; integer parameters as derived by
+ * load_cpu_decoder, sigcomp/cpu_int_inference.py:395-445).
+ *
+ *   embedding   int8  [257][emb_dim]            quantised embedding table
+ *   in_dims/out_dims [num_layers]               layer l is out_dims[l] x in_dims[l]
+ *   weights[l]  int8  [out_dims[l]][in_dims[l]] row-major
+ *   biases[l]   int32 [out_dims[l]]
+ *   multipliers int64 [num_layers]  M0 in [0, 2^31]
+ *   shifts      int32 [num_layers]  in [0, 63]
+ *   relu        uint8 [num_layers]
+ *   exp_lut     int64 [256]         build_integer_exp_lut(output_scale)
+ *   chunk_len   maximum tokens per chunk (SigComp -L/--chunk-len)
+ * Requirements: in_dims[0] == window * emb_dim, out_dims[last] == 256.
+ */
+SC_API int sc_model_create(int device, int32_t window, int32_t emb_dim, int32_t num_layers,
+                    const int8_t *embedding, const int32_t *in_dims, const int32_t *out_dims,
+                    const int8_t *const *weights, const int32_t *const *biases,
+                    const int64_t *multipliers, const int32_t *shifts, const uint8_t *relu,
+                    const int64_t *exp_lut, int32_t chunk_len, sc_model **out);
+
+/* Release the model and every device buffer it owns. */
+SC_API int sc_model_destroy(sc_model *model);
+
+/* Select the MLP implementation: 0 = automatic (tcgen05 when the geometry allows),
+ * 1 = tcgen05 tensor-core kernels, 2 = CUDA-core reference kernels. */
+SC_API int sc_model_set_mlp_path(sc_model *model, int32_t path);
+
+/*
+ * Compress chunks (host memory).  Replaces compress_chunks
+ * (sigcomp/quant_mlp_export.py:271-323; semantics of cpu_compression.py:178-257).
+ *   tokens         uint8 [token_offsets[n_chunks]]   concatenated chunks
+ *   token_offsets  int64 [n_chunks + 1]              chunk c = tokens[off[c] .. off[c+1])
+ *   words          uint32 [words_capacity]           output streams, concatenated
+ *   words_capacity >= sum over chunks of (length + 2) always suffices
+ *   word_offsets   int64 [n_chunks + 1]              output: stream c = words[wo[c] .. wo[c+1])
+ *   chunk_errors   uint8 [n_chunks] or NULL          output: 1 = coder capacity exceeded
+ * Empty chunks produce empty streams.
+ */
+SC_API int sc_compress_chunks(sc_model *model, const uint8_t *tokens, const int64_t *token_offsets,
+                       int64_t n_chunks, uint32_t *words, int64_t words_capacity,
+                       int64_t *word_offsets, uint8_t *chunk_errors, void *stream);
+
+/* Same as sc_compress_chunks with every array in device memory of the model's GPU. */
+SC_API int sc_compress_chunks_device(sc_model *model, const uint8_t *tokens, const int64_t *token_offsets,
+                              int64_t n_chunks, uint32_t *words, int64_t words_capacity,
+                              int64_t *word_offsets, uint8_t *chunk_errors, void *stream);
+
+/*
+ * Decompress chunks (host memory).  Replaces decompress_chunks
+ * (sigcomp/quant_mlp_export.py:325-377; semantics of cpu_compression.py:259-332).
+ *   words          uint32 [word_offsets[n_chunks]]
+ *   word_offsets   int64 [n_chunks + 1]
+ *   lengths        int64 [n_chunks]      tokens to decode per chunk, each in [0, chunk_len]
+ *   tokens         uint8 [sum(lengths)]  output, concatenated in chunk order
+ *   chunk_errors   uint8 [n_chunks] or NULL   output: 1 = invalid stream
+ * A chunk with length 0 must have an empty stream and vice versa, and every
+ * nonempty stream is decoded against its own word range only.
+ */
+SC_API int sc_decompress_chunks(sc_model *model, const uint32_t *words, const int64_t *word_offsets,
+                         const int64_t *lengths, int64_t n_chunks, uint8_t *tokens,
+                         uint8_t *chunk_errors, void *stream);
+
+/* Same as sc_decompress_chunks with words/word_offsets/lengths/tokens/chunk_errors
+ * in device memory.  `lengths_host` (host copy of lengths) must also be given. */
+SC_API int sc_decompress_chunks_device(sc_model *model, const uint32_t *words, const int64_t *word_offsets,
+                                const int64_t *lengths, const int64_t *lengths_host, int64_t n_chunks,
+                                uint8_t *tokens, uint8_t *chunk_errors, void *stream);
+
+/*
+ * The integer MLP alone on device memory: windows int16 [rows][window] (token
+ * ids in [0, 256]) -> logits int8 [rows][256].  Replaces the batched
+ * `_ar_step` of the GPU decoder (sigcomp/quant_mlp_export.py:125-130).
+ */
+SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t rows, int8_t *logits,
+                         void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SIGCOMP_B200_H */

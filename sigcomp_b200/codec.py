@@ -1,0 +1,262 @@
+"""The B200 codec object: a drop-in for SigComp's ``GPUCompression``.
+
+SigComp's ``_load_model`` (sigcomp/main.py:189-225) returns, for
+``--device cuda``, a ``GPUCompression(ReadFramingMixin, QuantMLPCompression)``
+object.  :class:`B200Compression` has the same constructor arguments,
+attributes (``chunk_len``, ``window_size``, ``SOS_token``, ``device``) and
+methods:
+
+* ``batch_inference_reads`` - read framing of ``ReadFramingMixin``
+  (sigcomp/cpu_compression.py:28-84), same validation and error messages;
+* ``compress_chunks`` / ``decompress_chunks`` - chunk codec with the byte-exact
+  semantics of the reference CPU backend (cpu_compression.py:178-332).
+
+All device work goes through the C ABI of ``libsigcomp_b200.so``.  There is no
+CPU fallback: without a B200 the constructor raises.
+"""
+
+import ctypes
+import struct
+
+import numpy as np
+
+from . import _lib
+from .model import IntModel, load_model
+
+_CHUNK_LENGTH = struct.Struct("<H")
+
+
+def _symbols(values):
+    """Validate one token sequence (cpu_compression.py:18-25)."""
+    values = np.asarray(values)
+    if values.ndim != 1:
+        raise ValueError("Each token sequence must be one-dimensional")
+    if values.size and (values.dtype.kind not in "iu" or np.any(values < 0) or np.any(values > 255)):
+        raise ValueError("Signal tokens must be integers in [0, 255]")
+    return np.ascontiguousarray(values, dtype=np.uint8)
+
+
+def _ptr(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else None
+
+
+class B200Compression:
+    DEFAULT_DIM = 256
+    DEFAULT_NUM_DEC_LAYERS = 8
+    DEFAULT_WINDOW_SIZE = 64
+
+    def __init__(self, chunk_len=1024, gpu=0, model_path=None, dim=None, num_dec_layers=None,
+                 window_size=None, *, model=None, mlp_path="auto"):
+        if chunk_len < 1 or chunk_len > 65535:
+            raise ValueError("chunk_len must be in [1, 65535]")
+        if model is None:
+            model = load_model(model_path, dim=dim or self.DEFAULT_DIM,
+                               num_dec_layers=num_dec_layers if num_dec_layers is not None
+                               else self.DEFAULT_NUM_DEC_LAYERS,
+                               window_size=window_size or self.DEFAULT_WINDOW_SIZE)
+        if not isinstance(model, IntModel):
+            raise TypeError("model must be an IntModel")
+        self.model = model
+        self.chunk_len = int(chunk_len)
+        self.window_size = int(model.window_size)
+        self.SOS_token = 256
+        self.gpu = int(gpu)
+        self.device = f"cuda:{self.gpu}"
+        self._lib = _lib.load()
+        self._handle = ctypes.c_void_p()
+        self._create(model)
+        self.set_mlp_path(mlp_path)
+
+    # -- model handle -----------------------------------------------------------
+    def _create(self, m):
+        emb = np.ascontiguousarray(m.embedding, dtype=np.int8)
+        ws = [np.ascontiguousarray(w, dtype=np.int8) for w in m.weights]
+        bs = [np.ascontiguousarray(b, dtype=np.int32) for b in m.biases]
+        in_dims = np.asarray([w.shape[1] for w in ws], dtype=np.int32)
+        out_dims = np.asarray([w.shape[0] for w in ws], dtype=np.int32)
+        w_ptrs = (ctypes.c_void_p * len(ws))(*[w.ctypes.data for w in ws])
+        b_ptrs = (ctypes.c_void_p * len(bs))(*[b.ctypes.data for b in bs])
+        mults = np.ascontiguousarray(m.multipliers, dtype=np.int64)
+        shifts = np.ascontiguousarray(m.shifts, dtype=np.int32)
+        relu = np.ascontiguousarray(m.relu, dtype=np.uint8)
+        lut = np.ascontiguousarray(m.exp_lut, dtype=np.int64)
+        rc = self._lib.sc_model_create(
+            self.gpu, self.window_size, emb.shape[1], len(ws), _ptr(emb), _ptr(in_dims), _ptr(out_dims),
+            ctypes.cast(w_ptrs, ctypes.c_void_p), ctypes.cast(b_ptrs, ctypes.c_void_p), _ptr(mults),
+            _ptr(shifts), _ptr(relu), _ptr(lut), self.chunk_len, ctypes.byref(self._handle))
+        _lib.check(rc, "sc_model_create")
+
+    def set_mlp_path(self, path):
+        code = {"auto": 0, "tcgen05": 1, "cuda_cores": 2}[path]
+        _lib.check(self._lib.sc_model_set_mlp_path(self._handle, code), "sc_model_set_mlp_path")
+        self.mlp_path = path
+
+    def close(self):
+        if getattr(self, "_handle", None) is not None and self._handle.value:
+            self._lib.sc_model_destroy(self._handle)
+            self._handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._handle
+
+    # -- flat (vectorised) entry points ----------------------------------------
+    def compress_flat(self, tokens, offsets, stream=None):
+        """tokens uint8[T], offsets int64[n+1] -> (words uint32[W], word_offsets int64[n+1])."""
+        tokens = np.ascontiguousarray(tokens, dtype=np.uint8)
+        offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+        n = len(offsets) - 1
+        lengths = np.diff(offsets)
+        cap = int(lengths.sum() + 2 * n) + 1
+        words = np.empty(cap, dtype=np.uint32)
+        word_offsets = np.zeros(n + 1, dtype=np.int64)
+        if n == 0:
+            return words[:0], word_offsets
+        rc = self._lib.sc_compress_chunks(self._handle, _ptr(tokens), _ptr(offsets), n, _ptr(words), cap,
+                                          _ptr(word_offsets), None, stream)
+        _lib.check(rc, "sc_compress_chunks")
+        return words[:int(word_offsets[-1])], word_offsets
+
+    def decompress_flat(self, words, word_offsets, lengths, stream=None):
+        """words uint32[W], word_offsets int64[n+1], lengths int64[n] -> tokens uint8[sum(lengths)]."""
+        words = np.ascontiguousarray(words, dtype=np.uint32)
+        word_offsets = np.ascontiguousarray(word_offsets, dtype=np.int64)
+        lengths = np.ascontiguousarray(lengths, dtype=np.int64)
+        n = len(lengths)
+        out = np.empty(max(int(lengths.sum()), 1), dtype=np.uint8)
+        if n == 0:
+            return out[:0]
+        if len(words) == 0:
+            words = np.zeros(1, dtype=np.uint32)
+        rc = self._lib.sc_decompress_chunks(self._handle, _ptr(words), _ptr(word_offsets), _ptr(lengths), n,
+                                            _ptr(out), None, stream)
+        _lib.check(rc, "sc_decompress_chunks")
+        return out[:int(lengths.sum())]
+
+    # -- chunk level (QuantMLPCompression interface) ---------------------------
+    def compress_chunks(self, chunks, max_batch_size=64, use_perfect=False, use_tqdm=False):
+        if max_batch_size < 1:
+            raise ValueError("max_batch_size must be positive")
+        batch = [_symbols(c) for c in chunks]
+        lengths = np.asarray([len(c) for c in batch], dtype=np.int64)
+        if np.any(lengths > self.chunk_len):
+            raise ValueError("A token chunk exceeds chunk_len")
+        if not len(batch):
+            return []
+        offsets = np.zeros(len(batch) + 1, dtype=np.int64)
+        np.cumsum(lengths, out=offsets[1:])
+        tokens = np.concatenate(batch) if offsets[-1] else np.zeros(0, np.uint8)
+        words, woff = self.compress_flat(tokens, offsets)
+        raw = words.astype("<u4", copy=False).view(np.uint8)
+        return [raw[4 * woff[c]:4 * woff[c + 1]].tobytes() for c in range(len(batch))]
+
+    def decompress_chunks(self, compressed_bytes_list, valid_lengths, max_batch_size=64, use_perfect=False,
+                          use_tqdm=False):
+        if max_batch_size < 1:
+            raise ValueError("max_batch_size must be positive")
+        if len(compressed_bytes_list) != len(valid_lengths):
+            raise ValueError("Compressed chunk and length counts differ")
+        if any(int(n) != n or n < 0 or n > self.chunk_len for n in valid_lengths):
+            raise ValueError("Chunk lengths must be integers in [0, chunk_len]")
+        for data, length in zip(compressed_bytes_list, valid_lengths):
+            if (length and (not data or len(data) % 4)) or (not length and data):
+                raise ValueError("Invalid range-coded chunk for its token length")
+        n = len(compressed_bytes_list)
+        if n == 0:
+            return []
+        lengths = np.asarray([int(x) for x in valid_lengths], dtype=np.int64)
+        nbytes = np.asarray([len(d) for d in compressed_bytes_list], dtype=np.int64)
+        woff = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(nbytes // 4, out=woff[1:])
+        blob = b"".join(bytes(d) for d in compressed_bytes_list)
+        words = np.frombuffer(blob, dtype="<u4").astype(np.uint32, copy=False)
+        tokens = self.decompress_flat(words, woff, lengths)
+        toff = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(lengths, out=toff[1:])
+        return [tokens[toff[c]:toff[c + 1]].copy() for c in range(n)]
+
+    # -- read level (ReadFramingMixin interface) -------------------------------
+    def batch_inference_reads(self, list_of_reads=None, list_of_compressed_reads=None, list_of_lengths=None,
+                              batch_size=64, use_tqdm=False, prob_quant=0):
+        if batch_size < 1:
+            raise ValueError("batch_size must be positive")
+        L = self.chunk_len
+        if list_of_reads is not None:
+            reads = [_symbols(r) for r in list_of_reads]
+            rlen = np.asarray([len(r) for r in reads], dtype=np.int64)
+            nchunks = (rlen + L - 1) // L
+            n = int(nchunks.sum())
+            tokens = np.concatenate(reads) if rlen.sum() else np.zeros(0, np.uint8)
+            # chunk boundaries: every read split into chunk_len pieces
+            read_start = np.zeros(len(reads) + 1, dtype=np.int64)
+            np.cumsum(rlen, out=read_start[1:])
+            chunk_read = np.repeat(np.arange(len(reads)), nchunks)
+            first_chunk = np.zeros(len(reads) + 1, dtype=np.int64)
+            np.cumsum(nchunks, out=first_chunk[1:])
+            k = np.arange(n) - first_chunk[chunk_read]
+            starts = read_start[chunk_read] + k * L
+            ends = np.minimum(starts + L, read_start[chunk_read + 1])
+            offsets = np.zeros(n + 1, dtype=np.int64)
+            if n:
+                offsets[:-1] = starts
+                offsets[-1] = ends[-1]
+            words, woff = self.compress_flat(tokens, offsets) if n else (np.zeros(0, np.uint32), offsets[:1])
+            nbytes = 4 * np.diff(woff)
+            if np.any(nbytes > 65535):
+                raise ValueError("Compressed chunk exceeds the SIG2 uint16 frame; compress with a smaller --chunk-len")
+            raw = words.astype("<u4", copy=False).view(np.uint8)
+            result = []
+            for r in range(len(reads)):
+                c0, c1 = int(first_chunk[r]), int(first_chunk[r + 1])
+                framed = bytearray()
+                for c in range(c0, c1):
+                    framed += _CHUNK_LENGTH.pack(int(nbytes[c]))
+                    framed += raw[4 * woff[c]:4 * woff[c + 1]].tobytes()
+                result.append(bytes(framed))
+            return result
+
+        if list_of_compressed_reads is None or list_of_lengths is None:
+            raise ValueError("Compressed reads and token lengths are required")
+        if len(list_of_compressed_reads) != len(list_of_lengths):
+            raise ValueError("Compressed read and token length counts differ")
+        chunks, lengths, mapping = [], [], []
+        for data, length in zip(list_of_compressed_reads, list_of_lengths):
+            if int(length) != length or length < 0:
+                raise ValueError("Token lengths must be nonnegative integers")
+            remaining, pos, begin = int(length), 0, len(chunks)
+            while remaining:
+                if pos + _CHUNK_LENGTH.size > len(data):
+                    raise ValueError("Truncated SIG2 chunk length")
+                size, = _CHUNK_LENGTH.unpack_from(data, pos)
+                pos += _CHUNK_LENGTH.size
+                if size == 0 or size % 4 or pos + size > len(data):
+                    raise ValueError("Invalid or truncated SIG2 range-coded chunk")
+                count = min(L, remaining)
+                chunks.append(data[pos:pos + size])
+                lengths.append(count)
+                pos += size
+                remaining -= count
+            if pos != len(data):
+                raise ValueError("Trailing SIG2 chunk data disagrees with token length")
+            mapping.append((begin, len(chunks)))
+        n = len(chunks)
+        if n == 0:
+            return [np.empty(0, dtype=np.uint8) for _ in mapping]
+        lengths = np.asarray(lengths, dtype=np.int64)
+        woff = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(np.asarray([len(c) // 4 for c in chunks], dtype=np.int64), out=woff[1:])
+        words = np.frombuffer(b"".join(bytes(c) for c in chunks), dtype="<u4").astype(np.uint32, copy=False)
+        tokens = self.decompress_flat(words, woff, lengths)
+        toff = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(lengths, out=toff[1:])
+        return [tokens[toff[b]:toff[e]].copy() if e > b else np.empty(0, dtype=np.uint8) for b, e in mapping]
+
+
+# The name SigComp's _load_model builds for --device cuda.
+GPUCompression = B200Compression

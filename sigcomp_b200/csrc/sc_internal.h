@@ -1,0 +1,87 @@
+// Internal declarations shared by the sigcomp_b200 translation units.
+#pragma once
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+#include <vector>
+#include <cuda_runtime.h>
+
+#include "sc_common.cuh"
+
+struct sc_model;
+
+namespace sc {
+
+// Thread-local error message used by sc_last_error().
+void set_error(const char *fmt, ...);
+void count_launch(int64_t n = 1);
+
+struct CudaError {
+    cudaError_t code;
+    std::string where;
+};
+
+#define SC_CUDA(call)                                                              \
+    do {                                                                           \
+        cudaError_t _e = (call);                                                   \
+        if (_e != cudaSuccess) throw ::sc::CudaError{_e, std::string(#call) + " at " + \
+                                                     __FILE__ + ":" + std::to_string(__LINE__)}; \
+    } while (0)
+
+#define SC_LAUNCH_CHECK() SC_CUDA(cudaGetLastError())
+
+// A grow-only device buffer owned by a model.
+struct DevBuf {
+    void *ptr = nullptr;
+    size_t bytes = 0;
+    void *get(size_t need, cudaStream_t s) {
+        if (need <= bytes) return ptr;
+        if (ptr) {
+            SC_CUDA(cudaStreamSynchronize(s));
+            SC_CUDA(cudaFree(ptr));
+            ptr = nullptr;
+            bytes = 0;
+        }
+        size_t cap = need < 4096 ? 4096 : need;
+        SC_CUDA(cudaMalloc(&ptr, cap));
+        bytes = cap;
+        return ptr;
+    }
+    void release() {
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr;
+        bytes = 0;
+    }
+};
+
+struct LayerDev {
+    int32_t in_dim, out_dim;
+    int8_t *w = nullptr;        // [out][in] row-major (CUDA-core path)
+    int8_t *w_tc = nullptr;     // tensor-core operand layout (tcgen05 path), or null
+    int32_t *bias = nullptr;    // [out]
+    Requant rq;
+};
+
+// Launch the CUDA-core MLP: windows int16 [rows][window] -> logits int8 [rows][256].
+void mlp_simple(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
+
+// Launch the tcgen05 MLP; returns false if unsupported for this model.
+bool mlp_tc_supported(const sc_model *m);
+void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
+void mlp_tc_prepare(sc_model *m);
+
+}  // namespace sc
+
+struct sc_model {
+    int device = 0;
+    int32_t window = 64, emb_dim = 128, num_layers = 0, chunk_len = 2048;
+    int32_t mlp_path = 0;      // 0 auto, 1 tcgen05, 2 CUDA cores
+    bool tc_ok = false;
+    int8_t *emb = nullptr;     // [257][emb_dim]
+    uint64_t *lut = nullptr;   // [256]
+    std::vector<sc::LayerDev> layers;
+    // workspaces
+    sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
+        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc;
+};

@@ -1,0 +1,208 @@
+"""GPU parity: the CUDA codec (through the C ABI) against the CPU oracle and the
+golden streams of the SigComp reference.  Bit-exact everywhere."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle.oracle import OracleModel
+
+pytestmark = pytest.mark.gpu
+
+PATHS = ["tcgen05", "cuda_cores"]
+
+
+def _chunks(z, tok="tokens", off="offsets"):
+    o = z[off]
+    return [z[tok][o[i]:o[i + 1]] for i in range(len(o) - 1)]
+
+
+def _streams(z):
+    o = z["word_offsets"]
+    return [z["words"][o[i]:o[i + 1]].astype("<u4").tobytes() for i in range(len(o) - 1)]
+
+
+_CODECS = {}
+
+
+def _codec(model, path="auto", chunk_len=2048):
+    from sigcomp_b200.codec import B200Compression
+    key = (model.name, id(model), chunk_len)
+    if key not in _CODECS:
+        _CODECS[key] = B200Compression(chunk_len=chunk_len, gpu=0, model=model)
+    c = _CODECS[key]
+    if path == "tcgen05" and not _tc_available(c):
+        pytest.skip("tcgen05 path not built for this geometry")
+    c.set_mlp_path(path)
+    return c
+
+
+def _tc_available(codec):
+    from sigcomp_b200 import _lib
+    rc = codec._lib.sc_model_set_mlp_path(codec.handle, 1)
+    codec._lib.sc_model_set_mlp_path(codec.handle, 0)
+    return rc == _lib.SC_OK
+
+
+def _gpu_logits(codec, windows):
+    import torch
+    w = torch.from_numpy(np.ascontiguousarray(windows, dtype=np.int16)).cuda()
+    out = torch.empty((len(windows), 256), dtype=torch.int8, device="cuda")
+    from sigcomp_b200 import _lib
+    rc = codec._lib.sc_mlp_logits_device(codec.handle, ctypes.c_void_p(w.data_ptr()), len(windows),
+                                         ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc)
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["lossless", "lossy"])
+@pytest.mark.parametrize("path", PATHS)
+def test_mlp_logits_match_reference_golden(golden, name, path, request):
+    model = request.getfixturevalue(f"{name}_model")
+    z = np.load(golden / f"mlp_{name}.npz")
+    assert np.array_equal(_gpu_logits(_codec(model, path), z["windows"]), z["logits"])
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("rows", [1, 127, 128, 129, 1000, 4099])
+def test_mlp_logits_random_model_match_oracle(path, rows):
+    from sigcomp_b200.model import random_model
+    model = random_model(11)
+    rng = np.random.default_rng(rows)
+    win = rng.integers(0, 257, size=(rows, 64)).astype(np.int16)
+    win[: rows // 3, : 20] = 256
+    got = _gpu_logits(_codec(model, path), win)
+    want = OracleModel(model).mlp(win)
+    assert np.array_equal(got, want)
+    # the random model must exercise both clamps of the final layer
+    assert (want == 127).any() or (want == -128).any() or rows < 128
+
+
+@pytest.mark.parametrize("name", ["lossless", "lossy"])
+@pytest.mark.parametrize("path", PATHS)
+def test_streams_match_reference_golden(golden, name, path, request):
+    model = request.getfixturevalue(f"{name}_model")
+    z = np.load(golden / f"streams_{name}.npz")
+    chunks, ref = _chunks(z), _streams(z)
+    codec = _codec(model, path)
+    assert codec.compress_chunks(chunks) == ref
+    back = codec.decompress_chunks(ref, [len(c) for c in chunks])
+    assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+
+
+@pytest.mark.parametrize("name", ["lossless", "lossy"])
+def test_read_framing_matches_reference_golden(golden, name, request):
+    model = request.getfixturevalue(f"{name}_model")
+    z = np.load(golden / f"streams_{name}.npz")
+    reads = _chunks(z, "read_tokens", "read_offsets")
+    framed_ref = [z["framed"][z["framed_offsets"][i]:z["framed_offsets"][i + 1]].tobytes()
+                  for i in range(len(reads))]
+    codec = _codec(model)
+    framed = codec.batch_inference_reads(list_of_reads=reads, batch_size=20480)
+    assert framed == framed_ref
+    back = codec.batch_inference_reads(list_of_compressed_reads=framed,
+                                       list_of_lengths=[len(r) for r in reads], batch_size=20480)
+    assert all(np.array_equal(a, b) for a, b in zip(back, reads))
+
+
+def test_edge_chunks(lossless_model):
+    codec = _codec(lossless_model)
+    rng = np.random.default_rng(5)
+    chunks = [np.empty(0, np.uint8), np.asarray([0], np.uint8), np.asarray([255], np.uint8),
+              rng.integers(0, 256, size=2048).astype(np.uint8), np.full(2048, 255, np.uint8),
+              np.zeros(2048, np.uint8), rng.integers(0, 3, size=65).astype(np.uint8), np.empty(0, np.uint8)]
+    streams = codec.compress_chunks(chunks)
+    assert streams[0] == b"" and streams[-1] == b""
+    assert streams == OracleModel(lossless_model).compress_chunks(chunks)
+    back = codec.decompress_chunks(streams, [len(c) for c in chunks])
+    assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+    assert codec.compress_chunks([]) == []
+    assert codec.decompress_chunks([], []) == []
+
+
+def test_reads_without_small_tokens(lossless_model):
+    codec = _codec(lossless_model)
+    reads = [np.empty(0, np.uint8), np.asarray([7, 9], np.uint8), np.empty(0, np.uint8)]
+    framed = codec.batch_inference_reads(list_of_reads=reads)
+    assert framed[0] == b"" and framed[2] == b""
+    back = codec.batch_inference_reads(list_of_compressed_reads=framed, list_of_lengths=[0, 2, 0])
+    assert [list(x) for x in back] == [[], [7, 9], []]
+
+
+def test_corrupt_stream_raises(lossless_model):
+    codec = _codec(lossless_model)
+    bad = np.asarray([0xFFFFFFFF, 0xFFFFFFFF], dtype="<u4").tobytes()   # quantile >= 2^24 at step 0
+    good = codec.compress_chunks([np.arange(50, dtype=np.uint8)])[0]
+    with pytest.raises(ValueError, match="invalid range stream"):
+        codec.decompress_chunks([good, bad], [50, 10])
+    with pytest.raises(ValueError, match="invalid range stream"):
+        OracleModel(lossless_model).decompress_chunks([good, bad], [50, 10])
+    # the model handle stays usable after a stream error
+    assert np.array_equal(codec.decompress_chunks([good], [50])[0], np.arange(50, dtype=np.uint8))
+
+
+def test_truncated_and_mismatched_streams_match_oracle(lossless_model):
+    codec = _codec(lossless_model)
+    om = OracleModel(lossless_model)
+    rng = np.random.default_rng(9)
+    chunks = [rng.integers(0, 30, size=n).astype(np.uint8) for n in (300, 1000, 2048)]
+    streams = codec.compress_chunks(chunks)
+    cases = [s[: 4 * max(1, len(s) // 8)] for s in streams]          # truncated streams
+    cases += [s[::-1][: len(s) - len(s) % 4] or s for s in streams]  # scrambled bytes
+    lengths = [len(c) for c in chunks] * 2
+    for data, n in zip(cases, lengths):
+        try:
+            want = om.decompress_chunks([data], [n])[0]
+        except ValueError:
+            with pytest.raises(ValueError):
+                codec.decompress_chunks([data], [n])
+            continue
+        assert np.array_equal(codec.decompress_chunks([data], [n])[0], want)
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_random_model_streams_match_oracle(path):
+    from sigcomp_b200.model import random_model
+    model = random_model(3)
+    rng = np.random.default_rng(3)
+    chunks = [rng.integers(0, 256, size=n).astype(np.uint8) for n in (1, 17, 128, 129, 2048, 700)]
+    codec = _codec(model, path)
+    om = OracleModel(model)
+    streams = codec.compress_chunks(chunks)
+    assert streams == om.compress_chunks(chunks)
+    back = codec.decompress_chunks(streams, [len(c) for c in chunks])
+    assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+
+
+def test_synthetic_reads_match_oracle(lossless_model):
+    from sigcomp_b200 import signal, synthetic
+    reads = synthetic.make_reads("r10_config1", seed=1, count=2)
+    toks = [signal.split_signal(r)[1] for r in reads]
+    chunks = []
+    for t in toks:
+        chunks += [t[i:i + 2048] for i in range(0, len(t), 2048)]
+    codec = _codec(lossless_model)
+    streams = codec.compress_chunks(chunks)
+    assert streams == OracleModel(lossless_model).compress_chunks(chunks, backend="int_mm")
+
+
+def test_large_round_trip_properties(lossless_model):
+    """Config-2-shaped reads at a size the oracle cannot check directly: round trip
+    identity, determinism, and agreement of the two MLP paths."""
+    from sigcomp_b200 import signal, synthetic
+    reads = synthetic.make_reads("r10_lognormal", seed=2, count=60)
+    toks = [signal.split_signal(r)[1] for r in reads]
+    codec = _codec(lossless_model)
+    lengths = [len(t) for t in toks]
+    framed = codec.batch_inference_reads(list_of_reads=toks, batch_size=20480)
+    assert framed == codec.batch_inference_reads(list_of_reads=toks, batch_size=20480)
+    back = codec.batch_inference_reads(list_of_compressed_reads=framed, list_of_lengths=lengths)
+    assert all(np.array_equal(a, b) for a, b in zip(back, toks))
+    if _tc_available(codec):
+        codec.set_mlp_path("cuda_cores")
+        assert codec.batch_inference_reads(list_of_reads=toks[:8]) == framed[:8]
+        codec.set_mlp_path("auto")
+    bits = 8 * sum(len(f) for f in framed) / sum(lengths)
+    assert 4.0 < bits < 8.0

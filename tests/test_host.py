@@ -1,0 +1,129 @@
+"""Host-side logic that needs no GPU: C-ABI exports, signal transform, synthetic
+data, framing validation and error mapping."""
+
+import re
+import ctypes
+
+import numpy as np
+import pytest
+
+from sigcomp_b200 import _lib, signal, synthetic
+from conftest import REPO
+
+
+def _declared_symbols():
+    names = set()
+    for h in (REPO / "include").glob("*.h"):
+        names |= set(re.findall(r"^SC_API[^(]*?\b(sc_\w+)\s*\(", h.read_text(), flags=re.M))
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    declared = _declared_symbols()
+    assert {"sc_model_create", "sc_compress_chunks", "sc_decompress_chunks", "sc_last_error"} <= declared
+    lib = ctypes.CDLL(str(_lib.LIB_PATH))
+    for name in sorted(declared):
+        assert hasattr(lib, name), name
+    assert set(_lib.EXPORTS) <= declared
+    L = _lib.load()
+    assert L.sc_version().decode().startswith("sigcomp_b200")
+
+
+def test_status_codes_map_to_reference_exceptions():
+    with pytest.raises(ValueError):
+        _lib.check(_lib.SC_ERR_INVALID_ARGUMENT)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.SC_ERR_CORRUPT_STREAM)
+    with pytest.raises(OverflowError):
+        _lib.check(_lib.SC_ERR_CAPACITY)
+    with pytest.raises(_lib.CodecError):
+        _lib.check(_lib.SC_ERR_CUDA)
+    _lib.check(_lib.SC_OK)
+
+
+def test_model_create_without_gpu_fails_cleanly(lossless_model):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from sigcomp_b200.codec import B200Compression
+    with pytest.raises((_lib.CodecError, ValueError)):
+        B200Compression(chunk_len=2048, model=lossless_model)
+
+
+def test_split_signal_matches_reference(golden):
+    z = np.load(golden / "signal.npz")
+    i = 0
+    while f"sig{i}" in z.files:
+        sig0, small, large, pos = signal.split_signal(z[f"sig{i}"])
+        assert sig0 == int(z[f"sig0_{i}"][0])
+        assert np.array_equal(small, z[f"small{i}"]) and small.dtype == np.uint8
+        assert np.array_equal(large, z[f"large{i}"])
+        assert np.array_equal(pos, z[f"pos{i}"])
+        lossy = signal.lossy_encode(signal.reduce_lsb(z[f"sig{i}"], 3), 3)
+        assert np.array_equal(lossy, z[f"lossy{i}"])
+        assert np.array_equal(signal.lossy_decode(lossy, 3), z[f"lossy_dec{i}"])
+        n = len(z[f"sig{i}"])
+        back = signal.reassemble_signal(sig0, n, small, large, pos)
+        assert np.array_equal(back, z[f"sig{i}"])
+        i += 1
+    assert i >= 3
+
+
+def test_synthetic_reads_are_seeded():
+    a = synthetic.make_reads("r10_lognormal", seed=3, count=5)
+    b = synthetic.make_reads("r10_lognormal", seed=3, count=5)
+    assert all(np.array_equal(x, y) for x, y in zip(a, b))
+    assert all(2000 <= len(x) <= 1_000_000 for x in a)
+    c = synthetic.make_reads("r10_config1", seed=0, count=2)
+    assert [len(x) for x in c] == [20000, 20000]
+    x = c[0].astype(np.float64)
+    assert 350 < x.mean() < 650
+    toks = signal.split_signal(c[0])[1]
+    assert len(toks) > 0.95 * (len(c[0]) - 1)       # deltas are overwhelmingly small
+
+
+class _FramingOnly:
+    """Exercises the framing validation of B200Compression without a device."""
+
+    def __new__(cls):
+        from sigcomp_b200.codec import B200Compression
+        obj = object.__new__(B200Compression)
+        obj.chunk_len = 4
+        obj.window_size = 64
+        obj.SOS_token = 256
+        return obj
+
+
+def test_framing_validation_errors():
+    codec = _FramingOnly()
+    with pytest.raises(ValueError, match="batch_size"):
+        codec.batch_inference_reads(list_of_reads=[np.zeros(3, np.uint8)], batch_size=0)
+    with pytest.raises(ValueError, match="integers in"):
+        codec.batch_inference_reads(list_of_reads=[np.asarray([1, 300])])
+    with pytest.raises(ValueError, match="one-dimensional"):
+        codec.batch_inference_reads(list_of_reads=[np.zeros((2, 2), np.uint8)])
+    with pytest.raises(ValueError, match="required"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b""])
+    with pytest.raises(ValueError, match="counts differ"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b""], list_of_lengths=[1, 2])
+    with pytest.raises(ValueError, match="Truncated"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b"\x04"], list_of_lengths=[3])
+    with pytest.raises(ValueError, match="Invalid or truncated"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b"\x03\x00abc"], list_of_lengths=[3])
+    with pytest.raises(ValueError, match="Trailing"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b"\x04\x00abcdxx"], list_of_lengths=[3])
+    with pytest.raises(ValueError, match="nonnegative"):
+        codec.batch_inference_reads(list_of_compressed_reads=[b""], list_of_lengths=[-1])
+    # empty reads need no device work
+    assert [len(x) for x in codec.batch_inference_reads(list_of_compressed_reads=[b"", b""],
+                                                        list_of_lengths=[0, 0])] == [0, 0]
+    with pytest.raises(ValueError, match="chunk_len"):
+        codec.decompress_chunks([b"abcd"], [5])
+    with pytest.raises(ValueError, match="token length"):
+        codec.decompress_chunks([b""], [3])
+    with pytest.raises(ValueError, match="token length"):
+        codec.decompress_chunks([b"abcd"], [0])
+    with pytest.raises(ValueError, match="counts differ"):
+        codec.decompress_chunks([b"abcd"], [1, 2])
+    with pytest.raises(ValueError, match="exceeds chunk_len"):
+        codec.compress_chunks([np.zeros(5, np.uint8)])
