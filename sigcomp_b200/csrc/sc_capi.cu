@@ -54,7 +54,12 @@ int guarded(sc_model *m, F &&f)
 {
     try {
         DeviceGuard g(m->device);
-        return f();
+        int rc = f();
+        if (read_device_error(1)) {
+            set_error("a device-side wait timed out (kernel gave up after its time limit)");
+            return SC_ERR_CUDA;
+        }
+        return rc;
     } catch (const CudaError &e) {
         return map_cuda(e);
     } catch (const std::bad_alloc &) {

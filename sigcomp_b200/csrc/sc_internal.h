@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <string>
 #include <vector>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "sc_common.cuh"
@@ -71,6 +72,9 @@ bool mlp_tc_supported(const sc_model *m);
 void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
 void mlp_tc_prepare(sc_model *m);
 
+// Value of the device error flag set by timed-out waits (optionally cleared).
+int read_device_error(int clear);
+
 }  // namespace sc
 
 struct sc_model {
@@ -81,6 +85,7 @@ struct sc_model {
     int8_t *emb = nullptr;     // [257][emb_dim]
     uint64_t *lut = nullptr;   // [256]
     std::vector<sc::LayerDev> layers;
+    std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
         ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc;

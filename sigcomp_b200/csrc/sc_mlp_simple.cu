@@ -9,7 +9,7 @@
 namespace sc {
 namespace {
 
-constexpr int BM = 64, BN = 64, BK = 64, PAD = 4;
+constexpr int BM = 64, BN = 64, BK = 64, PAD = 16;   // row stride 80 B keeps 16-byte stores aligned
 
 template <bool GATHER>
 __global__ void __launch_bounds__(256) k_linear_dp4a(
