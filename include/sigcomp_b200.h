@@ -133,6 +133,19 @@ SC_API int sc_decompress_chunks_device(sc_model *model, const uint32_t *words, c
 SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t rows, int8_t *logits,
                          void *stream);
 
+/*
+ * Per-launch CUDA-event timing (no counterpart in the reference; instrumentation
+ * for the benchmark's roofline).  sc_profile_enable(m, 1) resets the counters and
+ * starts recording an event pair around every launch on its own stream;
+ * sc_profile_read returns, for one kernel class, the summed device time, the
+ * number of launches and the work units (rows or chunks) they processed.
+ * Kernel classes: 0 context windows, 1 MLP layer 0, 2 hidden layers, 3 last
+ * layer, 4 frequency/symbol selection, 5 range encoder, 6 stream compaction,
+ * 7 decoder step.
+ */
+SC_API int sc_profile_enable(sc_model *model, int32_t enable);
+SC_API int sc_profile_read(sc_model *model, int32_t kind, double *total_ms, int64_t *launches, int64_t *work);
+
 #ifdef __cplusplus
 }
 #endif

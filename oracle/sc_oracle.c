@@ -399,3 +399,69 @@ int sco_decode_chunk_logits(const uint32_t *words, int64_t n, const int8_t *logi
     }
     return 0;
 }
+
+/* ---- batched autoregressive decoding (for the int_mm CPU baseline) -------
+ * Mirrors the loop of decompress_chunks (cpu_compression.py:310-323): the MLP
+ * of all active chunks runs as one batch per step, then every chunk decodes
+ * one symbol. */
+
+void *sco_dec_batch_create(const uint32_t *words, const int64_t *word_offsets, int64_t n)
+{
+    sco_decoder *d = (sco_decoder *)malloc(sizeof(sco_decoder) * (size_t)(n > 0 ? n : 1));
+    for (int64_t c = 0; c < n; ++c)
+        sco_decoder_init(&d[c], words + word_offsets[c], word_offsets[c + 1] - word_offsets[c]);
+    return d;
+}
+
+void sco_dec_batch_free(void *h) { free(h); }
+
+void sco_dec_batch_windows(const uint8_t *tokens, const int64_t *tok_off, const int64_t *idx, int64_t n_act,
+                           int64_t t, int32_t window, int16_t *out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n_act; ++i) {
+        const uint8_t *src = tokens + tok_off[idx[i]];
+        for (int p = 0; p < window; ++p) {
+            int64_t s = t - window + p;
+            out[i * window + p] = s < 0 ? SCO_SOS : src[s];
+        }
+    }
+}
+
+/* returns the number of chunks that failed at this step */
+int64_t sco_dec_batch_step(void *h, const int8_t *logits, const int64_t *idx, int64_t n_act, const int64_t *lut,
+                           uint8_t *tokens, const int64_t *tok_off, int64_t t, uint8_t *errors)
+{
+    sco_decoder *d = (sco_decoder *)h;
+    int64_t failed = 0;
+#pragma omp parallel for schedule(static) reduction(+:failed)
+    for (int64_t i = 0; i < n_act; ++i) {
+        const int64_t c = idx[i];
+        int s;
+        if (sco_decode_symbol(&d[c], logits + i * SCO_VOCAB, lut, &s)) {
+            errors[c] = 1;
+            failed += 1;
+            continue;
+        }
+        tokens[tok_off[c] + t] = (uint8_t)s;
+    }
+    return failed;
+}
+
+/* Embedding gather of context windows: x[r][p*E + c] = E[win[r][p]][c]
+ * (_embedding_window_row, sigcomp/cpu_int_kernels.py:107-121). Returns 1 on an
+ * out-of-vocabulary token. */
+int sco_gather_windows(const sco_model *m, const int16_t *windows, int64_t rows, int8_t *x)
+{
+    const int E = m->emb_dim, W = m->window;
+    int bad = 0;
+#pragma omp parallel for schedule(static) reduction(|:bad)
+    for (int64_t r = 0; r < rows; ++r) {
+        for (int p = 0; p < W; ++p) {
+            const int tok = windows[r * W + p];
+            if (tok < 0 || tok > SCO_SOS) { bad = 1; continue; }
+            memcpy(x + (r * W + p) * E, m->embedding + (size_t)tok * E, (size_t)E);
+        }
+    }
+    return bad;
+}

@@ -21,8 +21,10 @@ SC_ERR_OUT_OF_MEMORY = 6
 EXPORTS = (
     "sc_version", "sc_last_error", "sc_kernel_launches", "sc_model_create", "sc_model_destroy",
     "sc_model_set_mlp_path", "sc_compress_chunks", "sc_compress_chunks_device", "sc_decompress_chunks",
-    "sc_decompress_chunks_device", "sc_mlp_logits_device",
+    "sc_decompress_chunks_device", "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read",
 )
+
+KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step")
 
 _lib = None
 
@@ -52,14 +54,30 @@ def load():
     L.sc_decompress_chunks.argtypes = [vp, vp, vp, vp, i64, vp, vp, vp]
     L.sc_decompress_chunks_device.argtypes = [vp, vp, vp, vp, vp, i64, vp, vp, vp]
     L.sc_mlp_logits_device.argtypes = [vp, vp, i64, vp, vp]
+    L.sc_profile_enable.argtypes = [vp, i32]
+    L.sc_profile_read.argtypes = [vp, i32, vp, vp, vp]
     for name in EXPORTS:
         getattr(L, name)
     for name in ("sc_model_create", "sc_model_destroy", "sc_model_set_mlp_path", "sc_compress_chunks",
                  "sc_compress_chunks_device", "sc_decompress_chunks", "sc_decompress_chunks_device",
-                 "sc_mlp_logits_device"):
+                 "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L
+
+
+def profile_enable(handle, on=True):
+    check(load().sc_profile_enable(handle, 1 if on else 0), "sc_profile_enable")
+
+
+def profile_read(handle):
+    """{kind: (total_ms, launches, work)} for every kernel class."""
+    out = {}
+    for k, name in enumerate(KERNEL_KINDS):
+        ms, n, w = ctypes.c_double(), ctypes.c_int64(), ctypes.c_int64()
+        check(load().sc_profile_read(handle, k, ctypes.byref(ms), ctypes.byref(n), ctypes.byref(w)))
+        out[name] = (ms.value, n.value, w.value)
+    return out
 
 
 def last_error():

@@ -55,6 +55,10 @@ int guarded(sc_model *m, F &&f)
     try {
         DeviceGuard g(m->device);
         int rc = f();
+        if (m->prof.on) {
+            SC_CUDA(cudaDeviceSynchronize());
+            m->prof.collect();
+        }
         if (read_device_error(1)) {
             set_error("a device-side wait timed out (kernel gave up after its time limit)");
             return SC_ERR_CUDA;
@@ -402,6 +406,29 @@ int sc_decompress_chunks_device(sc_model *m, const uint32_t *words, const int64_
         }
         return SC_OK;
     });
+}
+
+int sc_profile_enable(sc_model *m, int32_t enable)
+{
+    if (!m) {
+        set_error("invalid model");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    m->prof.on = enable != 0;
+    m->prof.reset();
+    return SC_OK;
+}
+
+int sc_profile_read(sc_model *m, int32_t kind, double *total_ms, int64_t *launches, int64_t *work)
+{
+    if (!m || kind < 0 || kind >= KK_KINDS) {
+        set_error("invalid model or kernel kind");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    if (total_ms) *total_ms = m->prof.ms[kind];
+    if (launches) *launches = m->prof.launches[kind];
+    if (work) *work = m->prof.work[kind];
+    return SC_OK;
 }
 
 int sc_mlp_logits_device(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, void *stream)

@@ -266,18 +266,24 @@ int compress_device(sc_model *m, const uint8_t *tokens, const int64_t *off_d, co
             int16_t *win = (int16_t *)m->ws_windows.get(sizeof(int16_t) * rows * m->window, s);
             int8_t *logits = (int8_t *)m->ws_logits.get((size_t)rows * SC_VOCAB, s);
             dim3 g((unsigned)gn, (unsigned)std::max<int64_t>(1, std::min<int64_t>((max_len + 127) / 128, 16)));
+            ProfScope ps0(m->prof, KK_WINDOWS, s, rows);
             k_windows_compress<<<g, 128, 0, s>>>(tokens, off_d, c0, row_base, m->window, win);
             SC_LAUNCH_CHECK();
             count_launch();
             run_mlp(m, win, rows, logits, s);
+            ProfScope ps1(m->prof, KK_CDF, s, rows);
             k_cdf_select<<<(unsigned)std::min<int64_t>(blocks_for(rows, 8), 148 * 16), 256, 0, s>>>(
                 logits, tokens + row_base, m->lut, rows, pairs);
             SC_LAUNCH_CHECK();
             count_launch();
         }
+        {
+        ProfScope ps2(m->prof, KK_ENCODE, s, rows);
         k_encode<<<blocks_for(gn, 128), 128, 0, s>>>(pairs, off_d, c0, gn, row_base, stage, cap, nw, err);
         SC_LAUNCH_CHECK();
         count_launch();
+        }
+        ProfScope ps3(m->prof, KK_COMPACT, s, gn);
         size_t tmp_bytes = 0;
         SC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tmp_bytes, nw, incl, (int)gn, s));
         void *tmp = m->ws_scan.get(tmp_bytes, s);
@@ -343,11 +349,15 @@ int decompress_device(sc_model *m, const uint32_t *words, const int64_t *word_of
         int64_t n_act = g1 - g0;
         for (int64_t t = 0; t < gmax; ++t) {
             while (n_act > 0 && sorted_len[g0 + n_act - 1] <= t) --n_act;
+            {
+            ProfScope ps4(m->prof, KK_WINDOWS, s, n_act);
             k_windows_decode<<<blocks_for(n_act * m->window, 256), 256, 0, s>>>(tokens, tok_off_d, order_d + g0,
                                                                              n_act, t, m->window, win);
             SC_LAUNCH_CHECK();
             count_launch();
+            }
             run_mlp(m, win, n_act, logits, s);
+            ProfScope ps5(m->prof, KK_DECODE, s, n_act);
             k_decode_step<<<blocks_for(n_act, 8), 256, 0, s>>>(logits, m->lut, words, order_d + g0, tok_off_d,
                                                                n_act, t, st + g0, tokens, errors_d);
             SC_LAUNCH_CHECK();

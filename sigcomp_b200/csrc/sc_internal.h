@@ -56,6 +56,78 @@ struct DevBuf {
     }
 };
 
+// Kernel classes timed by the optional per-launch profiler (sc_profile_*).
+enum KernelKind {
+    KK_WINDOWS = 0, KK_LAYER0 = 1, KK_HIDDEN = 2, KK_LAST = 3, KK_CDF = 4, KK_ENCODE = 5,
+    KK_COMPACT = 6, KK_DECODE = 7, KK_KINDS = 8
+};
+
+// CUDA-event timing of individual launches on their own stream.  Disabled by
+// default; when enabled every timed launch records an event pair, and the pairs
+// are resolved after the API call has synchronised its stream.
+struct Profiler {
+    bool on = false;
+    struct Rec {
+        int kind;
+        cudaEvent_t a, b;
+        int64_t work;
+    };
+    std::vector<Rec> pending;
+    std::vector<cudaEvent_t> pool;
+    double ms[KK_KINDS] = {};
+    int64_t launches[KK_KINDS] = {};
+    int64_t work[KK_KINDS] = {};
+    cudaEvent_t ev() {
+        if (pool.empty()) {
+            cudaEvent_t e;
+            SC_CUDA(cudaEventCreate(&e));
+            return e;
+        }
+        cudaEvent_t e = pool.back();
+        pool.pop_back();
+        return e;
+    }
+    void reset() {
+        for (int k = 0; k < KK_KINDS; ++k) { ms[k] = 0; launches[k] = 0; work[k] = 0; }
+    }
+    void collect() {
+        for (auto &r : pending) {
+            float t = 0;
+            SC_CUDA(cudaEventElapsedTime(&t, r.a, r.b));
+            ms[r.kind] += t;
+            launches[r.kind] += 1;
+            work[r.kind] += r.work;
+            pool.push_back(r.a);
+            pool.push_back(r.b);
+        }
+        pending.clear();
+    }
+    ~Profiler() {
+        for (auto e : pool) cudaEventDestroy(e);
+        for (auto &r : pending) { cudaEventDestroy(r.a); cudaEventDestroy(r.b); }
+    }
+};
+
+struct ProfScope {
+    Profiler &p;
+    cudaStream_t s;
+    bool on;
+    Profiler::Rec rec;
+    ProfScope(Profiler &prof, int kind, cudaStream_t stream, int64_t work) : p(prof), s(stream), on(prof.on) {
+        if (!on) return;
+        rec.kind = kind;
+        rec.work = work;
+        rec.a = p.ev();
+        rec.b = p.ev();
+        SC_CUDA(cudaEventRecord(rec.a, s));
+    }
+    ~ProfScope() {
+        if (!on) return;
+        cudaEventRecord(rec.b, s);
+        p.pending.push_back(rec);
+    }
+};
+
 struct LayerDev {
     int32_t in_dim, out_dim;
     int8_t *w = nullptr;        // [out][in] row-major (CUDA-core path)
@@ -86,6 +158,7 @@ struct sc_model {
     uint64_t *lut = nullptr;   // [256]
     std::vector<sc::LayerDev> layers;
     std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path
+    sc::Profiler prof;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
         ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc;

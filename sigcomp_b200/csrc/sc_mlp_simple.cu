@@ -89,6 +89,7 @@ void mlp_simple(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logit
         const LayerDev &L = m->layers[l];
         int8_t *y = (l == m->num_layers - 1) ? logits : bufs[l & 1];
         dim3 grid((L.out_dim + BN - 1) / BN, (unsigned)((rows + BM - 1) / BM));
+        ProfScope ps(m->prof, l == 0 ? KK_LAYER0 : (l == m->num_layers - 1 ? KK_LAST : KK_HIDDEN), s, rows);
         if (l == 0)
             k_linear_dp4a<true><<<grid, 256, 0, s>>>(nullptr, windows, m->emb, m->emb_dim, m->window, L.w,
                                                      L.bias, L.rq, y, rows, L.out_dim, L.in_dim);

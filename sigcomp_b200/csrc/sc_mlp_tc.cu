@@ -251,6 +251,7 @@ void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, c
         const LayerDev &L = m->layers[l];
         int8_t *yb = (l == m->num_layers - 1) ? logits : bufs[l & 1];
         dim3 grid((unsigned)((rows + TM - 1) / TM), L.out_dim / TN);
+        ProfScope ps(m->prof, l == 0 ? KK_LAYER0 : (l == m->num_layers - 1 ? KK_LAST : KK_HIDDEN), s, rows);
         if (l == 0) {
             k_linear_tc<true><<<grid, 256, Cfg<true>::SMEM, s>>>(maps[0], maps[0], windows, m->window, m->emb, L.bias,
                                                                L.rq, yb, rows, L.out_dim, L.in_dim);
