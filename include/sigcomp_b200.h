@@ -81,7 +81,8 @@ SC_API int sc_model_create(int device, int32_t window, int32_t emb_dim, int32_t 
 SC_API int sc_model_destroy(sc_model *model);
 
 /* Select the MLP implementation: 0 = automatic (tcgen05 when the geometry allows),
- * 1 = tcgen05 tensor-core kernels, 2 = CUDA-core reference kernels. */
+ * 1 = tcgen05 fused persistent kernels on SM pairs (cta_group::2), 2 = CUDA-core
+ * kernels, 3 = tcgen05 one launch per layer, 4 = tcgen05 fused on single SMs. */
 SC_API int sc_model_set_mlp_path(sc_model *model, int32_t path);
 
 /*

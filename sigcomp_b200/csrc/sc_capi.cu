@@ -231,11 +231,11 @@ int sc_model_destroy(sc_model *m)
 
 int sc_model_set_mlp_path(sc_model *m, int32_t path)
 {
-    if (!m || path < 0 || path > 2) {
+    if (!m || path < 0 || path > 4) {
         set_error("invalid model or path");
         return SC_ERR_INVALID_ARGUMENT;
     }
-    if (path == 1 && !m->tc_ok) {
+    if ((path == 1 || path >= 3) && !m->tc_ok) {
         set_error("tcgen05 MLP path is not available for this model geometry");
         return SC_ERR_UNSUPPORTED;
     }

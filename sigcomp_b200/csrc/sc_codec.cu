@@ -226,13 +226,18 @@ inline unsigned blocks_for(int64_t n, int per) { return (unsigned)((n + per - 1)
 
 }  // namespace
 
+static bool use_tc(const sc_model *m) { return m->tc_ok && m->mlp_path != 2; }
+
 void run_mlp(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s)
 {
-    const bool tc = m->tc_ok && m->mlp_path != 2;
-    if (tc)
-        mlp_tc(m, windows, rows, logits, s);
-    else
+    if (use_tc(m)) {
+        L0Source src{};
+        src.kind = 1;
+        src.windows = windows;
+        mlp_tc(m, src, rows, 0, logits, s);
+    } else {
         mlp_simple(m, windows, rows, logits, s);
+    }
 }
 
 // Maximum MLP rows per pass (bounds the activation workspaces).
@@ -248,6 +253,7 @@ int compress_device(sc_model *m, const uint8_t *tokens, const int64_t *off_d, co
     count_launch();
     int *overflow = (int *)m->ws_misc.get(64, s);
     SC_CUDA(cudaMemsetAsync(overflow, 0, sizeof(int), s));
+    std::vector<int32_t> tile_c, tile_t;
     int64_t c0 = 0;
     while (c0 < n) {
         // group of chunks whose rows fit one pass (a chunk never exceeds chunk_len rows)
@@ -263,19 +269,53 @@ int compress_device(sc_model *m, const uint8_t *tokens, const int64_t *off_d, co
         uint32_t *stage = (uint32_t *)m->ws_stage.get(sizeof(uint32_t) * gn * cap, s);
         uint2 *pairs = (uint2 *)m->ws_pairs.get(sizeof(uint2) * std::max<int64_t>(rows, 1), s);
         if (rows > 0) {
-            int16_t *win = (int16_t *)m->ws_windows.get(sizeof(int16_t) * rows * m->window, s);
-            int8_t *logits = (int8_t *)m->ws_logits.get((size_t)rows * SC_VOCAB, s);
-            dim3 g((unsigned)gn, (unsigned)std::max<int64_t>(1, std::min<int64_t>((max_len + 127) / 128, 16)));
-            ProfScope ps0(m->prof, KK_WINDOWS, s, rows);
-            k_windows_compress<<<g, 128, 0, s>>>(tokens, off_d, c0, row_base, m->window, win);
-            SC_LAUNCH_CHECK();
-            count_launch();
-            run_mlp(m, win, rows, logits, s);
+            const bool fused = use_tc(m) && fused_supported(m);
+            int8_t *logits = fused ? nullptr : (int8_t *)m->ws_logits.get((size_t)rows * SC_VOCAB, s);
+            if (use_tc(m)) {
+                // 128-row tiles that never cross a chunk: layer 0 slides over each chunk's tokens
+                tile_c.clear();
+                tile_t.clear();
+                for (int64_t c = c0; c < c1; ++c)
+                    for (int64_t t0 = 0; t0 < off_h[c + 1] - off_h[c]; t0 += 128) {
+                        tile_c.push_back((int32_t)c);
+                        tile_t.push_back((int32_t)t0);
+                    }
+                const int64_t nt = (int64_t)tile_c.size();
+                int32_t *d_tiles = (int32_t *)m->ws_windows.get(sizeof(int32_t) * 2 * nt, s);
+                SC_CUDA(cudaMemcpyAsync(d_tiles, tile_c.data(), sizeof(int32_t) * nt, cudaMemcpyHostToDevice, s));
+                SC_CUDA(cudaMemcpyAsync(d_tiles + nt, tile_t.data(), sizeof(int32_t) * nt, cudaMemcpyHostToDevice, s));
+                if (fused) {
+                    // all layers + (cum, freq) selection in one persistent launch
+                    fused_compress(m, d_tiles, d_tiles + nt, nt, tokens, off_d, row_base, rows, pairs, s);
+                } else {
+                    L0Source src{};
+                    src.kind = 3;
+                    src.tokens = tokens;
+                    src.tok_off = off_d;
+                    src.tile_chunk = d_tiles;
+                    src.tile_t0 = d_tiles + nt;
+                    src.row_base = row_base;
+                    mlp_tc(m, src, rows, nt, logits, s);
+                }
+                SC_CUDA(cudaStreamSynchronize(s));   // tile lists are reused by the next group
+            } else {
+                int16_t *win = (int16_t *)m->ws_windows.get(sizeof(int16_t) * rows * m->window, s);
+                dim3 g((unsigned)gn, (unsigned)std::max<int64_t>(1, std::min<int64_t>((max_len + 127) / 128, 16)));
+                {
+                    ProfScope ps0(m->prof, KK_WINDOWS, s, rows);
+                    k_windows_compress<<<g, 128, 0, s>>>(tokens, off_d, c0, row_base, m->window, win);
+                    SC_LAUNCH_CHECK();
+                    count_launch();
+                }
+                mlp_simple(m, win, rows, logits, s);
+            }
+            if (!fused) {
             ProfScope ps1(m->prof, KK_CDF, s, rows);
             k_cdf_select<<<(unsigned)std::min<int64_t>(blocks_for(rows, 8), 148 * 16), 256, 0, s>>>(
                 logits, tokens + row_base, m->lut, rows, pairs);
             SC_LAUNCH_CHECK();
             count_launch();
+            }
         }
         {
         ProfScope ps2(m->prof, KK_ENCODE, s, rows);
@@ -339,24 +379,57 @@ int decompress_device(sc_model *m, const uint32_t *words, const int64_t *word_of
         set_error("Invalid range-coded chunk for its token length");
         return 1;
     }
+    if (use_tc(m) && fused_supported(m)) {
+        // persistent decoding: every launch keeps its chunks resident for all steps;
+        // chunks are split evenly over as few launches as the kernel's capacity allows
+        const int64_t cap = fused_decode_capacity(m);
+        const int64_t launches = (n + cap - 1) / cap;
+        const int64_t per = (n + launches - 1) / launches;
+        std::vector<int32_t> maxlen;
+        for (int64_t g0 = 0; g0 < n; g0 += per) {
+            const int64_t g1 = std::min(n, g0 + per);
+            if (sorted_len[g0] == 0) break;          // the rest are empty chunks
+            maxlen.clear();
+            int64_t work = 0;
+            for (int64_t j = g0; j < g1; j += 128) maxlen.push_back((int32_t)sorted_len[j]);
+            for (int64_t j = g0; j < g1; ++j) work += sorted_len[j];
+            int32_t *d_maxlen = (int32_t *)m->ws_windows.get(sizeof(int32_t) * maxlen.size(), s);
+            SC_CUDA(cudaMemcpyAsync(d_maxlen, maxlen.data(), sizeof(int32_t) * maxlen.size(), cudaMemcpyHostToDevice, s));
+            fused_decode(m, order_d + g0, g1 - g0, d_maxlen, lengths_d, st + g0, words, tokens, tok_off_d, errors_d,
+                         work, s);
+            SC_CUDA(cudaStreamSynchronize(s));       // tile lengths are rebuilt for the next launch
+        }
+        return 0;
+    }
     const int64_t max_rows = max_rows_per_pass(m);
     // process the ordered chunks in groups of at most max_rows concurrent chunks
     for (int64_t g0 = 0; g0 < n; g0 += max_rows) {
         const int64_t g1 = std::min(n, g0 + max_rows);
         const int64_t gmax = sorted_len[g0];
-        int16_t *win = (int16_t *)m->ws_windows.get(sizeof(int16_t) * (g1 - g0) * m->window, s);
+        int16_t *win = use_tc(m) ? nullptr
+                                 : (int16_t *)m->ws_windows.get(sizeof(int16_t) * (g1 - g0) * m->window, s);
         int8_t *logits = (int8_t *)m->ws_logits.get((size_t)(g1 - g0) * SC_VOCAB, s);
         int64_t n_act = g1 - g0;
         for (int64_t t = 0; t < gmax; ++t) {
             while (n_act > 0 && sorted_len[g0 + n_act - 1] <= t) --n_act;
-            {
-            ProfScope ps4(m->prof, KK_WINDOWS, s, n_act);
-            k_windows_decode<<<blocks_for(n_act * m->window, 256), 256, 0, s>>>(tokens, tok_off_d, order_d + g0,
-                                                                             n_act, t, m->window, win);
-            SC_LAUNCH_CHECK();
-            count_launch();
+            if (use_tc(m)) {
+                L0Source src{};
+                src.kind = 2;
+                src.tokens = tokens;
+                src.order = order_d + g0;
+                src.tok_off = tok_off_d;
+                src.t = t;
+                mlp_tc(m, src, n_act, 0, logits, s);
+            } else {
+                {
+                    ProfScope ps4(m->prof, KK_WINDOWS, s, n_act);
+                    k_windows_decode<<<blocks_for(n_act * m->window, 256), 256, 0, s>>>(
+                        tokens, tok_off_d, order_d + g0, n_act, t, m->window, win);
+                    SC_LAUNCH_CHECK();
+                    count_launch();
+                }
+                mlp_simple(m, win, n_act, logits, s);
             }
-            run_mlp(m, win, n_act, logits, s);
             ProfScope ps5(m->prof, KK_DECODE, s, n_act);
             k_decode_step<<<blocks_for(n_act, 8), 256, 0, s>>>(logits, m->lut, words, order_d + g0, tok_off_d,
                                                                n_act, t, st + g0, tokens, errors_d);

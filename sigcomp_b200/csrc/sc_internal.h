@@ -139,10 +139,35 @@ struct LayerDev {
 // Launch the CUDA-core MLP: windows int16 [rows][window] -> logits int8 [rows][256].
 void mlp_simple(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
 
-// Launch the tcgen05 MLP; returns false if unsupported for this model.
+// Where the rows of MLP layer 0 take their context windows from (tcgen05 path).
+struct L0Source {
+    int kind;                    // 1 explicit windows, 2 decode rows, 3 compress tiles
+    const int16_t *windows;      // kind 1: [rows][64]
+    const uint8_t *tokens;       // kind 2: decoded tokens; kind 3: the batch's tokens
+    const int64_t *order;        // kind 2: active row -> chunk
+    const int64_t *tok_off;      // kind 2: chunk -> first token; kind 3: token offsets of the chunks
+    int64_t t;                   // kind 2: decode step
+    const int32_t *tile_chunk;   // kind 3: chunk of each 128-row tile
+    const int32_t *tile_t0;      // kind 3: first position of each tile
+    int64_t row_base;            // kind 3: output row = tok_off[c] - row_base + t
+};
+
+// The tcgen05 MLP: layer 0 reads its windows as `src` describes, the other
+// layers stream activations through HBM; `l0_tiles` is the tile count of
+// compress tile lists (kind 3).
 bool mlp_tc_supported(const sc_model *m);
-void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
+void mlp_tc(sc_model *m, const L0Source &src, int64_t rows, int64_t l0_tiles, int8_t *logits, cudaStream_t s);
 void mlp_tc_prepare(sc_model *m);
+
+// Fused persistent kernels (all layers + coder step in one launch).
+bool fused_supported(const sc_model *m);
+int64_t fused_decode_capacity(const sc_model *m);
+void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_t0, int64_t n_tiles,
+                    const uint8_t *tokens, const int64_t *tok_off, int64_t row_base, int64_t rows, uint2 *pairs,
+                    cudaStream_t s);
+void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32_t *tile_maxlen,
+                  const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
+                  const int64_t *out_off, uint8_t *errors, int64_t work_rows, cudaStream_t s);
 
 // Value of the device error flag set by timed-out waits (optionally cleared).
 int read_device_error(int clear);
@@ -152,12 +177,16 @@ int read_device_error(int clear);
 struct sc_model {
     int device = 0;
     int32_t window = 64, emb_dim = 128, num_layers = 0, chunk_len = 2048;
-    int32_t mlp_path = 0;      // 0 auto, 1 tcgen05, 2 CUDA cores
+    // 0 auto, 1 tcgen05 (fused, CTA pairs), 2 CUDA cores, 3 tcgen05 layer by layer,
+    // 4 tcgen05 fused on single CTAs
+    int32_t mlp_path = 0;
+    int num_sms = 148;
     bool tc_ok = false;
     int8_t *emb = nullptr;     // [257][emb_dim]
     uint64_t *lut = nullptr;   // [256]
     std::vector<sc::LayerDev> layers;
-    std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path
+    std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path (box 256 rows)
+    std::vector<CUtensorMap> tc_wmaps2;  // weight tensor maps for CTA pairs (box 128 rows)
     sc::Profiler prof;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,

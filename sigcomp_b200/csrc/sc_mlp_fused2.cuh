@@ -1,0 +1,438 @@
+// Fused persistent MLP kernels on CTA pairs (tcgen05 cta_group::2).
+//
+// Same schedule and fused epilogues as the single-CTA kernels in
+// sc_mlp_fused.cuh, with every MMA spanning an SM pair: M = 256 rows (128 per
+// CTA), N = 256, so each SM loads only half of every weight tile and issues no
+// MMA of its own.  Included by sc_mlp_tc.cu (same translation unit as the
+// device error flag).
+//
+// Per pair:
+//   - both CTAs TMA-load their own activation rows and their half of the
+//     weight tile into the same shared-memory offsets, completing on the
+//     leader CTA's (rank 0) `full` barrier;
+//   - the leader issues the pair MMA and multicasts its commits to the
+//     `empty`, `acc_full` and `g_empty` barriers of both CTAs;
+//   - each CTA's epilogue warps read their own 128 TMEM lanes and arrive on the
+//     leader's `acc_empty` (remote arrive for the peer);
+//   - layer-0 builders (decode: activation stages, compress: sliding buffers)
+//     work on their own CTA's rows and arrive on the leader's barriers.
+// No TMA load uses cluster multicast.
+#pragma once
+
+namespace sc {
+
+constexpr int KT2 = 5;                // pair-tiles in flight per CTA pair
+
+struct Fused2Params {
+    CUtensorMap w[FMAX_LAYERS];       // weights, box 128 rows x 128 B (half of a 256-row unit)
+    CUtensorMap act[2];               // activation ping-pong, box 128 x 128 B
+    int8_t *act_ptr[2];
+    const int32_t *bias[FMAX_LAYERS];
+    Requant rq[FMAX_LAYERS];
+    int in_dim[FMAX_LAYERS];
+    int out_dim[FMAX_LAYERS];
+    int num_layers;
+    const int8_t *emb;
+    const uint64_t *lut;
+    int n_tiles;
+    // compress
+    const int32_t *tile_chunk;
+    const int32_t *tile_t0;
+    const int64_t *tok_off;
+    const uint8_t *tokens;
+    int64_t row_base;
+    uint2 *pairs;
+    // decode
+    const int64_t *order;
+    int64_t n_rows;
+    const int32_t *tile_maxlen;
+    const int64_t *lengths;
+    DecState *state;
+    const uint32_t *words;
+    uint8_t *tokens_out;
+    const int64_t *out_off;
+    uint8_t *errors;
+};
+
+namespace {
+
+constexpr int B_HALF = (TN / 2) * KB;          // 16 KB: this CTA's half of a weight K block
+constexpr int EPI_WARPS = 8;                    // epilogue warps per CTA (two per TMEM lane quarter)
+constexpr int BIAS_MAX = FMAX_LAYERS * MAX_N;   // int32 entries
+
+template <bool DECODE>
+struct F2Cfg {
+    static constexpr int STAGES = 4;
+    static constexpr int STAGE_BYTES = A_BYTES + B_HALF;                  // 32 KB
+    static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 128 KB
+    static constexpr int EMB_PAD = 33 * 1024;
+    static constexpr int RING_BYTES = TM * WIN;                           // 8 KB per slot
+    static constexpr int X_BYTES = DECODE ? EMB_PAD + KT2 * RING_BYTES : 2 * G_BYTES;
+    static constexpr int OFF_BIAS = OFF_X + X_BYTES;
+    static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
+    static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
+    static constexpr int NBAR = 2 * STAGES + 8;
+    static constexpr int OFF_CNT = OFF_BAR + NBAR * 8;
+    static constexpr int OFF_TMEM = OFF_CNT + 8 * 4;
+    static constexpr int SMEM = OFF_TMEM + 16 + 1024;
+};
+
+// Walk this pair's units in the fixed order both CTAs and every role follow.
+// Pair-tile pt covers tiles 2*pt (rank 0) and 2*pt+1 (rank 1).
+template <bool DECODE, typename F>
+__device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
+{
+    const int NP = gridDim.x / 2;
+    const int pair = blockIdx.x / 2;
+    const int n_pt = (p.n_tiles + 1) / 2;
+    const int my_pt = n_pt > pair ? (n_pt - 1 - pair) / NP + 1 : 0;
+    const int NL = p.num_layers;
+    for (int g0 = 0, grp = 0; g0 < my_pt; g0 += KT2, ++grp) {
+        const int gn = min(KT2, my_pt - g0);
+        int maxlen[KT2];
+        int steps = 1;
+#pragma unroll
+        for (int tt = 0; tt < KT2; ++tt) {
+            maxlen[tt] = 0;
+            if (tt < gn) {
+                // tiles are ordered by decreasing length: a pair-tile lasts as long as its first tile
+                maxlen[tt] = DECODE ? p.tile_maxlen[2 * (pair + (g0 + tt) * NP)] : 1;
+                steps = max(steps, maxlen[tt]);
+            }
+        }
+        for (int step = 0; step < steps; ++step)
+            for (int L = 0; L < NL; ++L)
+#pragma unroll 1
+                for (int tt = 0; tt < gn; ++tt) {
+                    if (DECODE && maxlen[tt] <= step) continue;
+                    const int pt = pair + (g0 + tt) * NP;
+                    const int NH = p.out_dim[L] / TN;
+                    for (int nh = 0; nh < NH; ++nh)
+                        if (!f(grp, tt, pt, step, L, nh)) return;
+                }
+    }
+}
+
+__device__ __forceinline__ void mma_k_block_pair(uint32_t d, uint32_t a_addr, uint32_t b_addr, bool first) {
+    constexpr uint32_t idesc = idesc_i8(2 * TM, TN);
+#pragma unroll
+    for (int k = 0; k < KB / 32; ++k)
+        mma_i8_pair(d, smem_desc_sw128(a_addr + 32 * k), smem_desc_sw128(b_addr + 32 * k), idesc,
+                    (!first || k) ? 1u : 0u);
+}
+
+template <bool DECODE>
+__global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused2Params p)
+{
+    using C = F2Cfg<DECODE>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
+    uint64_t *full = bars, *empty = bars + C::STAGES;
+    uint64_t *acc_full = bars + 2 * C::STAGES, *acc_empty = acc_full + 2;
+    uint64_t *g_full = acc_empty + 2, *g_empty = g_full + 2;
+    // act_cnt[tt]: +1 per epilogue warp of this CTA when its tile of slot tt finishes a
+    // layer; completion number k is reached at act_cnt[tt] >= EPI_WARPS * (k + 1)
+    uint32_t *act_cnt = (uint32_t *)(smem + C::OFF_CNT);
+    uint32_t *tmem_slot = (uint32_t *)(smem + C::OFF_TMEM);
+    int32_t *bias_s = (int32_t *)(smem + C::OFF_BIAS);
+    uint64_t *lut_s = (uint64_t *)(smem + C::OFF_LUT);
+    uint8_t *xbuf = smem + C::OFF_X;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int NL = p.num_layers;
+    const uint32_t rank = cluster_ctarank();
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::STAGES; ++s) {
+            mbar_init(&full[s], DECODE ? 1 + 4 : 1);   // leader producer (+ 2 builder warps x 2 CTAs)
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 2 * EPI_WARPS);
+            mbar_init(&g_full[b], 4);
+            mbar_init(&g_empty[b], 1);
+        }
+        for (int tt = 0; tt < 8; ++tt) act_cnt[tt] = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, 2 * TN);
+        tmem_relinquish_pair();
+    }
+    for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = p.lut[i];
+    for (int l = 0; l < NL; ++l)
+        for (int i = threadIdx.x; i < p.out_dim[l]; i += blockDim.x) bias_s[l * MAX_N + i] = p.bias[l][i];
+    if (DECODE) {
+        const int4 *srcv = reinterpret_cast<const int4 *>(p.emb);
+        int4 *dst = reinterpret_cast<int4 *>(xbuf);
+        for (int i = threadIdx.x; i < EMB_BYTES / 16; i += blockDim.x) dst[i] = srcv[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                       // both CTAs' barriers exist before any remote use
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int slot_row0 = blockIdx.x * KT2 * TM;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer (both CTAs): own activation rows + own half of the weights
+            uint32_t it = 0;
+            for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+                const int nkb = p.in_dim[L] / KB;
+                if (L >= 1 && nh == 0) {
+                    const uint32_t k = (uint32_t)((DECODE ? step : grp) * NL + L - 1);
+                    if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return false;
+                }
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return false;
+                    uint8_t *st = smem + s * C::STAGE_BYTES;
+                    const uint32_t fb = map_to_rank(&full[s], 0);
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (L == 0 ? 0 : A_BYTES)));
+                    if (L != 0) tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
+                    tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
+                }
+                return true;
+            });
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // ---- MMA issuer (leader CTA only)
+            uint32_t it = 0, uu = 0, li = 0;
+            for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+                const int nkb = p.in_dim[L] / KB;
+                const int ab = uu & 1;
+                if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
+                const int gb = li & 1;
+                if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
+                tc_fence_after();
+                const uint32_t d = tmem_base + ab * TN;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
+                    tc_fence_after();
+                    const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+                    const uint32_t a_addr = (!DECODE && L == 0) ? smem_u32(xbuf + gb * G_BYTES) + kb * KB : st;
+                    mma_k_block_pair(d, a_addr, st + A_BYTES, kb == 0);
+                    mma_commit_pair(&empty[s], 0x3);
+                }
+                mma_commit_pair(&acc_full[ab], 0x3);
+                ++uu;
+                if (!DECODE && L == 0 && nh == p.out_dim[0] / TN - 1) {
+                    mma_commit_pair(&g_empty[gb], 0x3);
+                    ++li;
+                }
+                return true;
+            });
+        }
+    } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
+        // ---- epilogue warps: TMEM lane quarter q; hidden layers split the 256 columns of
+        // a unit between the two warps of a quarter, the last layer runs on the first one
+        const int q = warp & 3;
+        const int half = (warp - 2) >> 2;
+        const int r = q * 32 + lane;
+        uint32_t uu = 0;
+        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+            const int ab = uu & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[ab], (uu >> 1) & 1))) return false;
+            ++uu;
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ab * TN + ((uint32_t)(q * 32) << 16);
+            const Requant rq = p.rq[L];
+            const int32_t *bias = bias_s + L * MAX_N;
+            const uint32_t acc_empty_leader = map_to_rank(&acc_empty[ab], 0);
+            const int tile = 2 * pt + (int)rank;
+            if (L < NL - 1) {
+                int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
+#pragma unroll 1
+                for (int c = half * 4; c < half * 4 + 4; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    tmem_ld_wait();
+                    uint32_t packed[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t w = 0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int col = nh * TN + c * 32 + i * 4 + b;
+                            const int32_t o = requant((int32_t)v[i * 4 + b], bias[col], rq);
+                            w |= ((uint32_t)(o & 0xFF)) << (8 * b);
+                        }
+                        packed[i] = w;
+                    }
+                    uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
+                    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                if (nh == p.out_dim[L] / TN - 1) {
+                    fence_proxy_async_global();
+                    __syncwarp();
+                    if (lane == 0) counter_add_release(&act_cnt[tt], 1);
+                }
+                return true;
+            }
+            if (half == 0) {
+                // last layer: requantise the 256 logits of this row and keep them packed in
+                // the first 64 columns of the same accumulator (already read)
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    tmem_ld_wait();
+                    uint32_t w8[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t w = 0;
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) {
+                            const int col = c * 32 + i * 4 + b;
+                            const int32_t o = requant((int32_t)v[i * 4 + b], bias[col], rq);
+                            w |= ((uint32_t)(o & 0xFF)) << (8 * b);
+                        }
+                        w8[i] = w;
+                    }
+                    tmem_st8(taddr + c * 8, w8);
+                }
+                tmem_st_wait();
+                // warp-collective TMEM passes: every lane runs them, rows without work
+                // compute on dummy inputs and store nothing
+                if (!DECODE) {
+                    const bool real_tile = tile < p.n_tiles;
+                    const int c = real_tile ? p.tile_chunk[tile] : 0;
+                    const int t0 = real_tile ? p.tile_t0[tile] : 0;
+                    const int64_t begin = p.tok_off[c];
+                    const bool valid = real_tile && t0 + r < p.tok_off[c + 1] - begin;
+                    const int sym = valid ? p.tokens[begin + t0 + r] : 0;
+                    int m, amax;
+                    RowDivisor d;
+                    uint32_t fix, cum, f;
+                    row_freq_stats(taddr, lut_s, m, d, fix, amax, sym, cum, f);
+                    if (valid) p.pairs[begin - p.row_base + t0 + r] = make_uint2(cum, f);
+                } else {
+                    const int64_t row = (int64_t)tile * TM + r;
+                    bool live = row < p.n_rows;
+                    const int64_t c = live ? p.order[row] : 0;
+                    live = live && step < p.lengths[c] && !p.errors[c];
+                    DecState s{};
+                    uint64_t scale = 0, qv = 0;
+                    if (live) {
+                        s = p.state[row];
+                        scale = s.range >> SC_PRECISION;
+                        qv = scale ? (s.point - s.lower) / scale : ~0ull;
+                        if (qv >= (uint64_t)SC_TOTAL) {      // invalid stream (cpu_entropy_coding.py:244-248)
+                            p.errors[c] = 1;
+                            live = false;
+                        }
+                    }
+                    int m, amax, sym;
+                    RowDivisor d;
+                    uint32_t fix, cum, f;
+                    row_freq_stats(taddr, lut_s, m, d, fix, amax, -1, cum, f);
+                    row_search(taddr, lut_s, m, d, fix, amax, live ? (uint32_t)qv : 0u, sym, cum, f);
+                    if (live) {
+                        s.lower += scale * (uint64_t)cum;
+                        s.range = scale * (uint64_t)f;
+                        if (s.range < (1ull << 32)) {
+                            s.lower <<= 32;
+                            s.range <<= 32;
+                            s.point <<= 32;
+                            if (s.read_pos < s.end_pos) s.point |= p.words[s.read_pos];
+                            s.read_pos += 1;
+                        }
+                        p.state[row] = s;
+                        p.tokens_out[p.out_off[c] + step] = (uint8_t)sym;
+                        uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
+                        ring[r * WIN + (step & (WIN - 1))] = (uint8_t)sym;
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive_cluster(acc_empty_leader);
+                counter_add_release(&act_cnt[tt], 1);
+            }
+            return true;
+        });
+    } else if (DECODE) {
+        // ---- warps 10-11: layer-0 activation stages of this CTA's rows from the embedding
+        // table and the window rings; they take part in every ring iteration
+        const int wb = (warp - 10) * 64;
+        const int j = lane & 7, sub = lane >> 3;
+        const uint8_t *emb_s = xbuf;
+        uint32_t it = 0;
+        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+            const int nkb = p.in_dim[L] / KB;
+            if (L == 0 && nh == 0 && step > 0) {
+                const uint32_t k = (uint32_t)(step * NL - 1);
+                if (!__all_sync(0xffffffffu, counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1)))) return false;
+            }
+            const uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % C::STAGES;
+                if (!__all_sync(0xffffffffu, mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)))
+                    return false;
+                if (L == 0) {
+                    uint8_t *a_st = smem + s * C::STAGE_BYTES;
+                    const int pos = step - WIN + kb;
+#pragma unroll 4
+                    for (int rr = sub; rr < 64; rr += 4) {
+                        const int rrow = wb + rr;
+                        const int tok = pos < 0 ? SC_SOS : ring[rrow * WIN + (pos & (WIN - 1))];
+                        const int4 v = *reinterpret_cast<const int4 *>(emb_s + tok * EMB_DIM + j * 16);
+                        *reinterpret_cast<int4 *>(a_st + sw128_offset(rrow, j)) = v;
+                    }
+                    fence_proxy_async_smem();
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(map_to_rank(&full[s], 0));
+            }
+            return true;
+        });
+    } else {
+        // ---- warps 10-11 (compress): sliding embedding buffer of this CTA's tile
+        const int tw = threadIdx.x - 320;        // 0..63
+        const int j = tw & 7, r0 = tw >> 3;
+        uint32_t li = 0;
+        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+            if (L != 0 || nh != 0) return true;
+            const int gb = li & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait_cluster(&g_empty[gb], ((li >> 1) & 1) ^ 1))) return false;
+            ++li;
+            uint8_t *g = xbuf + gb * G_BYTES;
+            const int tile = 2 * pt + (int)rank;
+            const bool real_tile = tile < p.n_tiles;
+            const int c = real_tile ? p.tile_chunk[tile] : 0;
+            const int t0 = real_tile ? p.tile_t0[tile] : 0;
+            const int64_t begin = p.tok_off[c];
+            const int64_t len = real_tile ? p.tok_off[c + 1] - begin : 0;
+#pragma unroll 4
+            for (int sr = r0; sr < G_ROWS; sr += 8) {
+                const int64_t pos = (int64_t)t0 - WIN + sr;
+                const int tok = pos < 0 ? SC_SOS : (pos < len ? p.tokens[begin + pos] : 0);
+                const int4 v = *reinterpret_cast<const int4 *>(p.emb + tok * EMB_DIM + j * 16);
+                *reinterpret_cast<int4 *>(g + sw128_offset(sr, j)) = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(map_to_rank(&g_full[gb], 0));
+            return true;
+        });
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();                       // no CTA leaves while its peer may still signal it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 2 * TN);
+    }
+}
+
+}  // namespace
+}  // namespace sc

@@ -18,6 +18,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+
 #include "sc_internal.h"
 #include "sc_tc.cuh"
 
@@ -27,161 +29,317 @@ namespace {
 using namespace tc;
 
 constexpr int TM = 128;          // rows per tile
-constexpr int TN = 256;          // output columns per tile
+constexpr int TN = 256;          // output columns per unit (one TMEM accumulator)
 constexpr int KB = 128;          // bytes of K per stage
 constexpr int A_BYTES = TM * KB;             // 16 KB
 constexpr int B_BYTES = TN * KB;             // 32 KB
 constexpr int EMB_ROWS = 257;
 constexpr int EMB_DIM = 128;
 constexpr int EMB_BYTES = EMB_ROWS * EMB_DIM;
+constexpr int WIN = 64;                      // context window of the tensor-core path
+constexpr int WS = WIN + 2;                  // window-token row stride (uint16): avoids bank conflicts
+constexpr int G_ROWS = TM + WIN;             // sliding-window embedding rows per tile
+constexpr int G_BYTES = G_ROWS * KB;         // 24 KB
+constexpr int MAX_N = 512;
 
-template <bool GATHER>
+// A operand sources
+enum { A_TMA = 0, A_GATHER = 1, A_SLIDE = 3 };
+
+template <int MODE>
 struct Cfg {
-    static constexpr int STAGES = GATHER ? 3 : 4;
-    static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    static constexpr int OFF_EMB = STAGES * STAGE_BYTES;
-    static constexpr int OFF_BIAS = OFF_EMB + (GATHER ? ((EMB_BYTES + 1023) / 1024) * 1024 : 0);
-    static constexpr int OFF_BAR = OFF_BIAS + TN * 4;
-    static constexpr int OFF_TMEM = OFF_BAR + (2 * STAGES + 2) * 8;
+    static constexpr int STAGES = MODE == A_GATHER ? 3 : 4;
+    static constexpr int STAGE_BYTES = (MODE == A_SLIDE ? 0 : A_BYTES) + B_BYTES;
+    static constexpr int OFF_EXTRA = STAGES * STAGE_BYTES;
+    // A_GATHER: embedding table + window tokens; A_SLIDE: two sliding buffers
+    static constexpr int EXTRA = MODE == A_GATHER ? (33 * 1024 + TM * WS * 2)
+                               : MODE == A_SLIDE ? 2 * G_BYTES : 0;
+    static constexpr int OFF_BIAS = OFF_EXTRA + EXTRA;
+    static constexpr int OFF_BAR = OFF_BIAS + MAX_N * 4;
+    static constexpr int NBAR = 2 * STAGES + 8;
+    static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;   // + alignment slack
 };
 
-template <bool GATHER>
-__global__ void __launch_bounds__(256, 1) k_linear_tc(
-    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
-    const int16_t *__restrict__ windows, int window, const int8_t *__restrict__ emb,
-    const int32_t *__restrict__ bias, Requant rq, int8_t *__restrict__ y, int64_t M, int N, int K)
+}  // namespace
+
+namespace {
+
+__device__ __forceinline__ void mma_k_block(uint32_t d, uint32_t a_addr, uint32_t b_addr, bool first) {
+    constexpr uint32_t idesc = idesc_i8(TM, TN);
+#pragma unroll
+    for (int k = 0; k < KB / 32; ++k)
+        mma_i8(d, smem_desc_sw128(a_addr + 32 * k), smem_desc_sw128(b_addr + 32 * k), idesc,
+               (!first || k) ? 1u : 0u);
+}
+
+// Persistent layer kernel: every CTA walks row tiles blockIdx.x, +gridDim.x, ...
+// and for each tile the N/256 output halves ("units").  Two TMEM accumulators
+// (2 x 256 columns) let the epilogue of one unit overlap the MMAs of the next.
+//   warp 0      TMA producer (weights; activations in A_TMA mode)
+//   warp 1      TMEM owner; lane 0 issues tcgen05.mma and commits
+//   warps 2-5   epilogue (TMEM lane quarters 2,3,0,1)
+//   warps 6-7   A_GATHER: build activation stages from the embedding table;
+//               A_SLIDE: build the per-tile sliding embedding buffer
+template <int MODE>
+__global__ void __launch_bounds__(256, 1) k_layer(
+    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, const L0Source src,
+    const int8_t *__restrict__ emb, const int32_t *__restrict__ bias, Requant rq, int8_t *__restrict__ y,
+    int64_t M, int N, int K, int n_tiles)
 {
-    using C = Cfg<GATHER>;
+    using C = Cfg<MODE>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = (uint64_t *)(smem + C::OFF_BAR);
-    uint64_t *empty = full + C::STAGES;
-    uint64_t *acc_full = empty + C::STAGES;
+    uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
+    uint64_t *full = bars, *empty = bars + C::STAGES;
+    uint64_t *acc_full = bars + 2 * C::STAGES, *acc_empty = acc_full + 2;
+    uint64_t *g_full = acc_empty + 2, *g_empty = g_full + 2;
     uint32_t *tmem_slot = (uint32_t *)(smem + C::OFF_TMEM);
     int32_t *bias_s = (int32_t *)(smem + C::OFF_BIAS);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t m0 = (int64_t)blockIdx.x * TM;
-    const int n0 = blockIdx.y * TN;
+    const int NH = N / TN;
     const int nkb = K / KB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], GATHER ? 1 + 64 : 1);
+            mbar_init(&full[s], MODE == A_GATHER ? 1 + 2 : 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 4);
+            mbar_init(&g_full[b], 2);
+            mbar_init(&g_empty[b], 1);
+        }
         fence_mbar_init();
         prefetch_tmap(&tmap_w);
-        if (!GATHER) prefetch_tmap(&tmap_x);
+        if (MODE == A_TMA) prefetch_tmap(&tmap_x);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TN);
+        tmem_alloc(tmem_slot, 2 * TN);
         tmem_relinquish();
     }
-    for (int i = threadIdx.x; i < TN; i += blockDim.x) bias_s[i] = bias[n0 + i];
-    if (GATHER) {
-        const int4 *src = reinterpret_cast<const int4 *>(emb);
-        int4 *dst = reinterpret_cast<int4 *>(smem + C::OFF_EMB);
-        for (int i = threadIdx.x; i < EMB_BYTES / 16; i += blockDim.x) dst[i] = src[i];
+    for (int i = threadIdx.x; i < N; i += blockDim.x) bias_s[i] = bias[i];
+    if (MODE == A_GATHER) {
+        const int4 *srcv = reinterpret_cast<const int4 *>(emb);
+        int4 *dst = reinterpret_cast<int4 *>(smem + C::OFF_EXTRA);
+        for (int i = threadIdx.x; i < EMB_BYTES / 16; i += blockDim.x) dst[i] = srcv[i];
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem_acc = *tmem_slot;
+    const uint32_t tmem_base = *tmem_slot;
 
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % C::STAGES;
-            const uint32_t ph = (kb / C::STAGES) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1)) break;
-            uint8_t *a_st = smem + s * C::STAGE_BYTES;
-            uint8_t *b_st = a_st + A_BYTES;
-            mbar_arrive_expect_tx(&full[s], GATHER ? B_BYTES : B_BYTES + A_BYTES);
-            tma_load_2d(b_st, &tmap_w, &full[s], kb * KB, n0);
-            if (!GATHER) tma_load_2d(a_st, &tmap_x, &full[s], kb * KB, (int32_t)m0);
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---- TMA producer
+            uint32_t it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x)
+                for (int nh = 0; nh < NH && ok; ++nh)
+                    for (int kb = 0; kb < nkb; ++kb, ++it) {
+                        const int s = it % C::STAGES;
+                        if (!(ok = mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1))) break;
+                        uint8_t *st = smem + s * C::STAGE_BYTES;
+                        if (MODE == A_TMA) {
+                            mbar_arrive_expect_tx(&full[s], A_BYTES + B_BYTES);
+                            tma_load_2d(st, &tmap_x, &full[s], kb * KB, tile * TM);
+                            tma_load_2d(st + A_BYTES, &tmap_w, &full[s], kb * KB, nh * TN);
+                        } else {
+                            mbar_arrive_expect_tx(&full[s], B_BYTES);
+                            tma_load_2d(st + (MODE == A_SLIDE ? 0 : A_BYTES), &tmap_w, &full[s], kb * KB, nh * TN);
+                        }
+                    }
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer
-        constexpr uint32_t idesc = idesc_i8(TM, TN);
-        bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % C::STAGES;
-            const uint32_t ph = (kb / C::STAGES) & 1;
-            if (!mbar_wait(&full[s], ph)) { ok = false; break; }
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(smem + s * C::STAGE_BYTES);
-            const uint32_t b_addr = a_addr + A_BYTES;
-#pragma unroll
-            for (int k = 0; k < KB / 32; ++k)
-                mma_i8(tmem_acc, smem_desc_sw128(a_addr + 32 * k), smem_desc_sw128(b_addr + 32 * k), idesc,
-                       (kb | k) != 0);
-            mma_commit(&empty[s]);
-        }
-        mma_commit(acc_full);
-        (void)ok;
-    } else if (GATHER && (warp == 2 || warp == 3)) {
-        // ---- activation-tile builders for layer 0
-        const int t = threadIdx.x - 64;       // 0..63
-        const int j = t & 7;                  // 16-byte chunk of the 128-byte row
-        const int r0 = t >> 3;                // first row, then every 8th
-        const uint8_t *emb_s = smem + C::OFF_EMB;
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % C::STAGES;
-            const uint32_t ph = (kb / C::STAGES) & 1;
-            if (!mbar_wait(&empty[s], ph ^ 1)) break;
-            uint8_t *a_st = smem + s * C::STAGE_BYTES;
-#pragma unroll 4
-            for (int r = r0; r < TM; r += 8) {
-                const int64_t row = m0 + r;
-                const int tok = row < M ? windows[row * window + kb] : 256;
-                const int4 v = *reinterpret_cast<const int4 *>(emb_s + tok * EMB_DIM + j * 16);
-                *reinterpret_cast<int4 *>(a_st + sw128_offset(r, j)) = v;
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---- MMA issuer
+            uint32_t it = 0, uu = 0, li = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++li) {
+                const int gb = li & 1;
+                if (MODE == A_SLIDE && !(ok = mbar_wait(&g_full[gb], (li >> 1) & 1))) break;
+                tc_fence_after();
+                for (int nh = 0; nh < NH && ok; ++nh, ++uu) {
+                    const int ab = uu & 1;
+                    if (!(ok = mbar_wait(&acc_empty[ab], ((uu >> 1) & 1) ^ 1))) break;
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + ab * TN;
+                    for (int kb = 0; kb < nkb; ++kb, ++it) {
+                        const int s = it % C::STAGES;
+                        if (!(ok = mbar_wait(&full[s], (it / C::STAGES) & 1))) break;
+                        tc_fence_after();
+                        const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+                        uint32_t a_addr, b_addr;
+                        if (MODE == A_SLIDE) {
+                            // K block kb is window position kb: rows kb .. kb+127 of the sliding buffer
+                            a_addr = smem_u32(smem + C::OFF_EXTRA + gb * G_BYTES) + kb * KB;
+                            b_addr = st;
+                        } else {
+                            a_addr = st;
+                            b_addr = st + A_BYTES;
+                        }
+                        mma_k_block(d, a_addr, b_addr, kb == 0);
+                        mma_commit(&empty[s]);
+                    }
+                    mma_commit(&acc_full[ab]);
+                }
+                if (MODE == A_SLIDE) mma_commit(&g_empty[gb]);
             }
-            fence_proxy_async_smem();
-            mbar_arrive(&full[s]);
         }
-    } else if (warp >= 4) {
-        // ---- epilogue
+    } else if (warp >= 2 && warp <= 5) {
+        // ---- epilogue: TMEM -> requantise -> int8 rows
         const int q = warp & 3;
         const int r = q * 32 + lane;
-        const int64_t row = m0 + r;
-        const bool ok = __all_sync(0xffffffffu, mbar_wait(acc_full, 0));
-        if (ok) {
-            tc_fence_after();
+        uint32_t uu = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            int64_t row;
+            bool valid;
+            if (MODE == A_SLIDE) {
+                const int c = src.tile_chunk[tile];
+                const int t0 = src.tile_t0[tile];
+                const int64_t len = src.tok_off[c + 1] - src.tok_off[c];
+                valid = t0 + r < len;
+                row = src.tok_off[c] - src.row_base + t0 + r;
+            } else {
+                row = (int64_t)tile * TM + r;
+                valid = row < M;
+            }
+            for (int nh = 0; nh < NH; ++nh, ++uu) {
+                const int ab = uu & 1;
+                ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[ab], (uu >> 1) & 1));
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ab * TN + ((uint32_t)(q * 32) << 16);
 #pragma unroll 1
-            for (int c = 0; c < TN / 32; ++c) {
-                uint32_t v[32];
-                tmem_ld32(tmem_acc + ((uint32_t)(q * 32) << 16) + c * 32, v);
-                tmem_ld_wait();
-                uint32_t packed[8];
+                for (int c = 0; c < TN / 32; ++c) {
+                    uint32_t v[32];
+                    tmem_ld32(taddr + c * 32, v);
+                    tmem_ld_wait();
+                    uint32_t packed[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    uint32_t p = 0;
+                    for (int i = 0; i < 8; ++i) {
+                        uint32_t p = 0;
 #pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        const int col = c * 32 + i * 4 + b;
-                        const int32_t o = requant((int32_t)v[i * 4 + b], bias_s[col], rq);
-                        p |= ((uint32_t)(o & 0xFF)) << (8 * b);
+                        for (int b = 0; b < 4; ++b) {
+                            const int col = nh * TN + c * 32 + i * 4 + b;
+                            const int32_t o = requant((int32_t)v[i * 4 + b], bias_s[col], rq);
+                            p |= ((uint32_t)(o & 0xFF)) << (8 * b);
+                        }
+                        packed[i] = p;
                     }
-                    packed[i] = p;
+                    if (valid) {
+                        uint4 *dst = reinterpret_cast<uint4 *>(y + row * N + nh * TN + c * 32);
+                        dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                        dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    }
                 }
-                if (row < M) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(y + row * N + n0 + c * 32);
-                    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[ab]);
+            }
+        }
+    } else if (MODE == A_GATHER) {
+        // ---- warps 6-7: activation stages from the embedding table; warp 6 builds
+        // rows 0-63, warp 7 rows 64-127, each from its own window tokens
+        const int wb = (warp - 6) * 64;
+        const uint8_t *emb_s = smem + C::OFF_EXTRA;
+        uint16_t *win_s = (uint16_t *)(smem + C::OFF_EXTRA + 33 * 1024);
+        const int j = lane & 7, sub = lane >> 3;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+            // window tokens of this warp's 64 rows: lane handles rows wb+lane and wb+lane+32
+            __syncwarp();
+            for (int h = 0; h < 2; ++h) {
+                const int r = wb + lane + 32 * h;
+                const int64_t row = (int64_t)tile * TM + r;
+                uint16_t *dst = win_s + r * WS;
+                if (row >= M) {
+                    for (int p = 0; p < WIN; ++p) dst[p] = SC_SOS;
+                } else if (src.kind == 1) {
+                    const int4 *w = reinterpret_cast<const int4 *>(src.windows + row * WIN);
+#pragma unroll
+                    for (int v = 0; v < WIN / 8; ++v) {
+                        const int4 x = w[v];
+                        const uint32_t xs[4] = {(uint32_t)x.x, (uint32_t)x.y, (uint32_t)x.z, (uint32_t)x.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            dst[v * 8 + 2 * e] = (uint16_t)(xs[e] & 0xFFFF);
+                            dst[v * 8 + 2 * e + 1] = (uint16_t)(xs[e] >> 16);
+                        }
+                    }
+                } else {
+                    const int64_t b0 = src.tok_off[src.order[row]];
+#pragma unroll 16
+                    for (int p = 0; p < WIN; ++p) {
+                        const int64_t pos = src.t - WIN + p;
+                        dst[p] = pos >= 0 ? (uint16_t)src.tokens[b0 + pos] : (uint16_t)SC_SOS;
+                    }
                 }
             }
+            __syncwarp();
+            for (int nh = 0; nh < NH && ok; ++nh)
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % C::STAGES;
+                    ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1));
+                    if (!ok) break;
+                    uint8_t *a_st = smem + s * C::STAGE_BYTES;
+#pragma unroll 4
+                    for (int rr = sub; rr < 64; rr += 4) {
+                        const int r = wb + rr;
+                        const int tok = win_s[r * WS + kb];
+                        const int4 v = *reinterpret_cast<const int4 *>(emb_s + tok * EMB_DIM + j * 16);
+                        *reinterpret_cast<int4 *>(a_st + sw128_offset(r, j)) = v;
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[s]);
+                }
+        }
+    } else if (MODE == A_SLIDE) {
+        // ---- warps 6-7: sliding embedding buffer of the tile: row s holds
+        // E_q[token at position t0 - 64 + s] (SOS before the chunk start), so the
+        // activation of K block p is rows p .. p+127 of the buffer
+        const int tw = threadIdx.x - 192;        // 0..63
+        const int j = tw & 7, r0 = tw >> 3;
+        uint32_t li = 0;
+        for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++li) {
+            const int gb = li & 1;
+            if (!__all_sync(0xffffffffu, mbar_wait(&g_empty[gb], ((li >> 1) & 1) ^ 1))) break;
+            uint8_t *g = smem + C::OFF_EXTRA + gb * G_BYTES;
+            const int c = src.tile_chunk[tile];
+            const int t0 = src.tile_t0[tile];
+            const int64_t begin = src.tok_off[c];
+            const int64_t len = src.tok_off[c + 1] - begin;
+#pragma unroll 4
+            for (int sr = r0; sr < G_ROWS; sr += 8) {
+                const int64_t pos = (int64_t)t0 - WIN + sr;
+                const int tok = pos < 0 ? SC_SOS : (pos < len ? src.tokens[begin + pos] : 0);
+                const int4 v = *reinterpret_cast<const int4 *>(emb + tok * EMB_DIM + j * 16);
+                *reinterpret_cast<int4 *>(g + sw128_offset(sr, j)) = v;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&g_full[gb]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_acc, TN);
+        tmem_dealloc(tmem_base, 2 * TN);
     }
 }
+
+}  // namespace
+}  // namespace sc
+
+#include "sc_mlp_fused.cuh"
+#include "sc_mlp_fused2.cuh"
+
+namespace sc {
+namespace {
 
 // ---- host side ------------------------------------------------------------------
 
@@ -217,10 +375,16 @@ CUtensorMap make_tmap(const void *base, uint64_t cols, uint64_t rows, uint64_t p
 
 bool mlp_tc_supported(const sc_model *m)
 {
-    if (m->emb_dim != EMB_DIM || m->window * EMB_DIM != m->layers[0].in_dim) return false;
+    if (m->emb_dim != EMB_DIM || m->window != WIN || m->layers[0].in_dim != WIN * EMB_DIM) return false;
     for (auto &L : m->layers)
-        if (L.in_dim % KB || L.out_dim % TN) return false;
+        if (L.in_dim % KB || L.out_dim % TN || L.out_dim > MAX_N) return false;
     return true;
+}
+
+template <int MODE>
+static void set_smem_attr()
+{
+    SC_CUDA(cudaFuncSetAttribute(k_layer<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<MODE>::SMEM));
 }
 
 void mlp_tc_prepare(sc_model *m)
@@ -228,15 +392,20 @@ void mlp_tc_prepare(sc_model *m)
     auto &maps = m->tc_wmaps;
     maps.clear();
     for (auto &L : m->layers) maps.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, TN));
-    static bool attr = false;
-    if (!attr) {
-        SC_CUDA(cudaFuncSetAttribute(k_linear_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<true>::SMEM));
-        SC_CUDA(cudaFuncSetAttribute(k_linear_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<false>::SMEM));
-        attr = true;
-    }
+    set_smem_attr<A_TMA>();
+    set_smem_attr<A_GATHER>();
+    set_smem_attr<A_SLIDE>();
+    SC_CUDA(cudaFuncSetAttribute(k_fused<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FCfg<true>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<true>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<false>::SMEM));
+    auto &maps2 = m->tc_wmaps2;
+    maps2.clear();
+    for (auto &L : m->layers) maps2.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, TN / 2));
+    SC_CUDA(cudaFuncSetAttribute(k_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FCfg<false>::SMEM));
+    SC_CUDA(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
 }
 
-void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s)
+void mlp_tc(sc_model *m, const L0Source &src, int64_t rows, int64_t l0_tiles, int8_t *logits, cudaStream_t s)
 {
     if (rows <= 0) return;
     auto &maps = m->tc_wmaps;
@@ -246,24 +415,183 @@ void mlp_tc(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, c
         (int8_t *)m->ws_act0.get((size_t)rows * max_w, s),
         (int8_t *)m->ws_act1.get((size_t)rows * max_w, s),
     };
+    const int64_t row_tiles = (rows + TM - 1) / TM;
     const int8_t *x = nullptr;
     for (int l = 0; l < m->num_layers; ++l) {
         const LayerDev &L = m->layers[l];
         int8_t *yb = (l == m->num_layers - 1) ? logits : bufs[l & 1];
-        dim3 grid((unsigned)((rows + TM - 1) / TM), L.out_dim / TN);
         ProfScope ps(m->prof, l == 0 ? KK_LAYER0 : (l == m->num_layers - 1 ? KK_LAST : KK_HIDDEN), s, rows);
         if (l == 0) {
-            k_linear_tc<true><<<grid, 256, Cfg<true>::SMEM, s>>>(maps[0], maps[0], windows, m->window, m->emb, L.bias,
-                                                               L.rq, yb, rows, L.out_dim, L.in_dim);
+            const int64_t nt = src.kind == 3 ? l0_tiles : row_tiles;
+            const unsigned grid = (unsigned)std::min<int64_t>(nt, m->num_sms);
+            if (src.kind == 3)
+                k_layer<A_SLIDE><<<grid, 256, Cfg<A_SLIDE>::SMEM, s>>>(maps[0], maps[0], src, m->emb, L.bias, L.rq,
+                                                                      yb, rows, L.out_dim, L.in_dim, (int)nt);
+            else
+                k_layer<A_GATHER><<<grid, 256, Cfg<A_GATHER>::SMEM, s>>>(maps[0], maps[0], src, m->emb, L.bias, L.rq,
+                                                                        yb, rows, L.out_dim, L.in_dim, (int)nt);
         } else {
             CUtensorMap xm = make_tmap(x, L.in_dim, rows, L.in_dim, TM);
-            k_linear_tc<false><<<grid, 256, Cfg<false>::SMEM, s>>>(maps[l], xm, nullptr, 0, nullptr, L.bias, L.rq,
-                                                                 yb, rows, L.out_dim, L.in_dim);
+            const unsigned grid = (unsigned)std::min<int64_t>(row_tiles, m->num_sms);
+            k_layer<A_TMA><<<grid, 256, Cfg<A_TMA>::SMEM, s>>>(maps[l], xm, src, m->emb, L.bias, L.rq, yb, rows,
+                                                              L.out_dim, L.in_dim, (int)row_tiles);
         }
         SC_LAUNCH_CHECK();
         count_launch();
         x = yb;
     }
+}
+
+// Shared parameters of the fused kernels; activation buffers are sized for
+// grid * KT tiles of 128 rows.
+static void fused_common(sc_model *m, FusedParams &p, int grid, cudaStream_t s)
+{
+    const int64_t rows = (int64_t)grid * KT * TM;
+    int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
+    int8_t *a1 = (int8_t *)m->ws_act1.get((size_t)rows * MAX_N, s);
+    p.act_ptr[0] = a0;
+    p.act_ptr[1] = a1;
+    p.act[0] = make_tmap(a0, MAX_N, rows, MAX_N, TM);
+    p.act[1] = make_tmap(a1, MAX_N, rows, MAX_N, TM);
+    p.num_layers = m->num_layers;
+    for (int l = 0; l < m->num_layers; ++l) {
+        p.w[l] = m->tc_wmaps[l];
+        p.bias[l] = m->layers[l].bias;
+        p.rq[l] = m->layers[l].rq;
+        p.in_dim[l] = m->layers[l].in_dim;
+        p.out_dim[l] = m->layers[l].out_dim;
+    }
+    p.emb = m->emb;
+    p.lut = m->lut;
+}
+
+bool fused_supported(const sc_model *m) { return m->tc_ok && m->num_layers <= FMAX_LAYERS && m->mlp_path != 3; }
+
+static bool use_pairs(const sc_model *m) { return m->mlp_path != 4 && m->num_sms >= 2; }
+
+int64_t fused_decode_capacity(const sc_model *m)
+{
+    return use_pairs(m) ? (int64_t)(m->num_sms / 2) * KT2 * 2 * TM : (int64_t)m->num_sms * KT * TM;
+}
+
+static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s)
+{
+    const int64_t rows = (int64_t)grid * KT2 * TM;
+    int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
+    int8_t *a1 = (int8_t *)m->ws_act1.get((size_t)rows * MAX_N, s);
+    p.act_ptr[0] = a0;
+    p.act_ptr[1] = a1;
+    p.act[0] = make_tmap(a0, MAX_N, rows, MAX_N, TM);
+    p.act[1] = make_tmap(a1, MAX_N, rows, MAX_N, TM);
+    p.num_layers = m->num_layers;
+    for (int l = 0; l < m->num_layers; ++l) {
+        p.w[l] = m->tc_wmaps2[l];
+        p.bias[l] = m->layers[l].bias;
+        p.rq[l] = m->layers[l].rq;
+        p.in_dim[l] = m->layers[l].in_dim;
+        p.out_dim[l] = m->layers[l].out_dim;
+    }
+    p.emb = m->emb;
+    p.lut = m->lut;
+}
+
+template <bool DECODE>
+static void launch_pairs(const Fused2Params &p, int grid, cudaStream_t s)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(384);
+    cfg.dynamicSmemBytes = F2Cfg<DECODE>::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    SC_CUDA(cudaLaunchKernelEx(&cfg, k_fused2<DECODE>, p));
+}
+
+void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_t0, int64_t n_tiles,
+                    const uint8_t *tokens, const int64_t *tok_off, int64_t row_base, int64_t rows, uint2 *pairs,
+                    cudaStream_t s)
+{
+    if (n_tiles <= 0) return;
+    ProfScope ps(m->prof, KK_LAYER0, s, rows);
+    if (use_pairs(m)) {
+        const int64_t n_pt = (n_tiles + 1) / 2;
+        const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);
+        Fused2Params p{};
+        fused2_common(m, p, grid, s);
+        p.n_tiles = (int)n_tiles;
+        p.tile_chunk = tile_chunk;
+        p.tile_t0 = tile_t0;
+        p.tok_off = tok_off;
+        p.tokens = tokens;
+        p.row_base = row_base;
+        p.pairs = pairs;
+        launch_pairs<false>(p, grid, s);
+    } else {
+        const int grid = (int)std::min<int64_t>(n_tiles, m->num_sms);
+        FusedParams p{};
+        fused_common(m, p, grid, s);
+        p.n_tiles = (int)n_tiles;
+        p.tile_chunk = tile_chunk;
+        p.tile_t0 = tile_t0;
+        p.tok_off = tok_off;
+        p.tokens = tokens;
+        p.row_base = row_base;
+        p.pairs = pairs;
+        k_fused<false><<<grid, 256, FCfg<false>::SMEM, s>>>(p);
+    }
+    SC_LAUNCH_CHECK();
+    count_launch();
+}
+
+void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32_t *tile_maxlen,
+                  const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
+                  const int64_t *out_off, uint8_t *errors, int64_t work_rows, cudaStream_t s)
+{
+    if (n_rows <= 0) return;
+    const int64_t n_tiles = (n_rows + TM - 1) / TM;
+    ProfScope ps(m->prof, KK_DECODE, s, work_rows);
+    if (use_pairs(m)) {
+        const int64_t n_pt = (n_tiles + 1) / 2;
+        const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);
+        if (n_pt > (int64_t)(grid / 2) * KT2) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        Fused2Params p{};
+        fused2_common(m, p, grid, s);
+        p.n_tiles = (int)n_tiles;
+        p.order = order;
+        p.n_rows = n_rows;
+        p.tile_maxlen = tile_maxlen;
+        p.lengths = lengths;
+        p.state = state;
+        p.words = words;
+        p.tokens_out = tokens_out;
+        p.out_off = out_off;
+        p.errors = errors;
+        launch_pairs<true>(p, grid, s);
+    } else {
+        const int grid = (int)std::min<int64_t>(n_tiles, m->num_sms);
+        if (n_tiles > (int64_t)grid * KT) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        FusedParams p{};
+        fused_common(m, p, grid, s);
+        p.n_tiles = (int)n_tiles;
+        p.order = order;
+        p.n_rows = n_rows;
+        p.tile_maxlen = tile_maxlen;
+        p.lengths = lengths;
+        p.state = state;
+        p.words = words;
+        p.tokens_out = tokens_out;
+        p.out_off = out_off;
+        p.errors = errors;
+        k_fused<true><<<grid, 256, FCfg<true>::SMEM, s>>>(p);
+    }
+    SC_LAUNCH_CHECK();
+    count_launch();
 }
 
 int read_device_error(int clear)

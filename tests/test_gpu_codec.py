@@ -11,6 +11,9 @@ from oracle.oracle import OracleModel
 pytestmark = pytest.mark.gpu
 
 PATHS = ["tcgen05", "cuda_cores"]
+# every MLP implementation the library ships: fused on SM pairs, fused on single
+# SMs, one launch per layer, CUDA cores
+ALL_PATHS = ["tcgen05", "tcgen05_fused1", "tcgen05_layers", "cuda_cores"]
 
 
 def _chunks(z, tok="tokens", off="offsets"):
@@ -32,7 +35,7 @@ def _codec(model, path="auto", chunk_len=2048):
     if key not in _CODECS:
         _CODECS[key] = B200Compression(chunk_len=chunk_len, gpu=0, model=model)
     c = _CODECS[key]
-    if path == "tcgen05" and not _tc_available(c):
+    if path.startswith("tcgen05") and not _tc_available(c):
         pytest.skip("tcgen05 path not built for this geometry")
     c.set_mlp_path(path)
     return c
@@ -81,7 +84,7 @@ def test_mlp_logits_random_model_match_oracle(path, rows):
 
 
 @pytest.mark.parametrize("name", ["lossless", "lossy"])
-@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("path", ALL_PATHS)
 def test_streams_match_reference_golden(golden, name, path, request):
     model = request.getfixturevalue(f"{name}_model")
     z = np.load(golden / f"streams_{name}.npz")
@@ -162,7 +165,7 @@ def test_truncated_and_mismatched_streams_match_oracle(lossless_model):
         assert np.array_equal(codec.decompress_chunks([data], [n])[0], want)
 
 
-@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("path", ALL_PATHS)
 def test_random_model_streams_match_oracle(path):
     from sigcomp_b200.model import random_model
     model = random_model(3)
@@ -201,8 +204,9 @@ def test_large_round_trip_properties(lossless_model):
     back = codec.batch_inference_reads(list_of_compressed_reads=framed, list_of_lengths=lengths)
     assert all(np.array_equal(a, b) for a, b in zip(back, toks))
     if _tc_available(codec):
-        codec.set_mlp_path("cuda_cores")
-        assert codec.batch_inference_reads(list_of_reads=toks[:8]) == framed[:8]
+        for path in ("cuda_cores", "tcgen05_layers", "tcgen05_fused1"):
+            codec.set_mlp_path(path)
+            assert codec.batch_inference_reads(list_of_reads=toks[:8]) == framed[:8], path
         codec.set_mlp_path("auto")
     bits = 8 * sum(len(f) for f in framed) / sum(lengths)
     assert 4.0 < bits < 8.0
