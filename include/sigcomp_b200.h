@@ -147,6 +147,19 @@ SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t
 SC_API int sc_profile_enable(sc_model *model, int32_t enable);
 SC_API int sc_profile_read(sc_model *model, int32_t kind, double *total_ms, int64_t *launches, int64_t *work);
 
+/*
+ * Unit trace of the fused kernels (no counterpart in the reference; pipeline
+ * instrumentation).  With records_per_cta > 0 every later fused launch records,
+ * for the first SM pair, one 16-byte event per role and unit: word 0 is the GPU
+ * %globaltimer (ns), word 1 packs role | event << 4 | layer << 8 | half << 12 |
+ * slot << 16 | step << 32 (roles 0 producer, 1 MMA, 2 epilogue, 3 layer-0
+ * builders; events 0 begin, 1 dependency satisfied, 2 end).  0 disables.
+ * sc_trace_read copies up to `capacity` records of CTA 0 or 1 of the most
+ * recent launch and returns their number (-1 on error).
+ */
+SC_API int sc_trace_enable(sc_model *model, int32_t records_per_cta);
+SC_API int64_t sc_trace_read(sc_model *model, int32_t cta, uint64_t *records, int64_t capacity);
+
 #ifdef __cplusplus
 }
 #endif

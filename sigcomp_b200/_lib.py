@@ -22,6 +22,7 @@ EXPORTS = (
     "sc_version", "sc_last_error", "sc_kernel_launches", "sc_model_create", "sc_model_destroy",
     "sc_model_set_mlp_path", "sc_compress_chunks", "sc_compress_chunks_device", "sc_decompress_chunks",
     "sc_decompress_chunks_device", "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read",
+    "sc_trace_enable", "sc_trace_read",
 )
 
 KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step")
@@ -56,6 +57,10 @@ def load():
     L.sc_mlp_logits_device.argtypes = [vp, vp, i64, vp, vp]
     L.sc_profile_enable.argtypes = [vp, i32]
     L.sc_profile_read.argtypes = [vp, i32, vp, vp, vp]
+    L.sc_trace_enable.argtypes = [vp, i32]
+    L.sc_trace_enable.restype = ctypes.c_int
+    L.sc_trace_read.argtypes = [vp, i32, vp, i64]
+    L.sc_trace_read.restype = i64
     for name in EXPORTS:
         getattr(L, name)
     for name in ("sc_model_create", "sc_model_destroy", "sc_model_set_mlp_path", "sc_compress_chunks",

@@ -1,4 +1,5 @@
 // extern "C" boundary of libsigcomp_b200 (declared in include/sigcomp_b200.h).
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstring>
@@ -215,6 +216,8 @@ int sc_model_destroy(sc_model *m)
         cudaDeviceSynchronize();
         cudaFree(m->emb);
         cudaFree(m->lut);
+        cudaFree(m->trace_buf);
+        cudaFree(m->trace_count);
         for (auto &L : m->layers) {
             cudaFree(L.w);
             cudaFree(L.w_tc);
@@ -429,6 +432,44 @@ int sc_profile_read(sc_model *m, int32_t kind, double *total_ms, int64_t *launch
     if (launches) *launches = m->prof.launches[kind];
     if (work) *work = m->prof.work[kind];
     return SC_OK;
+}
+
+int sc_trace_enable(sc_model *m, int32_t records_per_cta)
+{
+    if (!m || records_per_cta < 0) {
+        set_error("invalid model or record count");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    return guarded(m, [&]() -> int {
+        cudaFree(m->trace_buf);
+        cudaFree(m->trace_count);
+        m->trace_buf = nullptr;
+        m->trace_count = nullptr;
+        m->trace_cap = 0;
+        if (records_per_cta > 0) {
+            SC_CUDA(cudaMalloc(&m->trace_buf, sizeof(unsigned long long) * 2 * 2 * (size_t)records_per_cta));
+            SC_CUDA(cudaMalloc(&m->trace_count, 2 * sizeof(unsigned int)));
+            SC_CUDA(cudaMemset(m->trace_count, 0, 2 * sizeof(unsigned int)));
+            m->trace_cap = records_per_cta;
+        }
+        return SC_OK;
+    });
+}
+
+int64_t sc_trace_read(sc_model *m, int32_t cta, uint64_t *records, int64_t capacity)
+{
+    if (!m || cta < 0 || cta > 1 || !m->trace_buf) return 0;
+    int64_t n = 0;
+    int rc = guarded(m, [&]() -> int {
+        unsigned int cnt[2] = {0, 0};
+        SC_CUDA(cudaMemcpy(cnt, m->trace_count, sizeof(cnt), cudaMemcpyDeviceToHost));
+        n = std::min<int64_t>(std::min<int64_t>(cnt[cta], m->trace_cap), capacity);
+        if (n > 0)
+            SC_CUDA(cudaMemcpy(records, m->trace_buf + (size_t)cta * m->trace_cap * 2, sizeof(uint64_t) * 2 * n,
+                               cudaMemcpyDeviceToHost));
+        return SC_OK;
+    });
+    return rc == SC_OK ? n : -1;
 }
 
 int sc_mlp_logits_device(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, void *stream)

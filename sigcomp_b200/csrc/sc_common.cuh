@@ -55,6 +55,34 @@ __device__ __forceinline__ int32_t requant(int32_t acc, int32_t bias, const Requ
     return (int32_t)scaled;
 }
 
+// Four requantised outputs packed as int8 (lowest column in the lowest byte).
+// Fast form for multipliers with the high-word path (M0 < 2^31, shift >= 32):
+// the int32 wrap of acc + bias, the high word of the 64-bit product and an
+// arithmetic shift give floor(biased * M0 / 2^shift); the lower bound (0 with
+// ReLU, else -128) is applied with max, and cvt.pack.sat saturates to 127.
+__device__ __forceinline__ uint32_t sat_pack4(int32_t r0, int32_t r1, int32_t r2, int32_t r3) {
+    uint32_t hi, d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(r3), "r"(r2), "r"(0));
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(r1), "r"(r0), "r"(hi));
+    return d;
+}
+
+__device__ __forceinline__ int32_t requant_hi(uint32_t acc, int32_t bias, int32_t m0, int32_t hs, int32_t lo) {
+    return max(__mulhi((int32_t)(acc + (uint32_t)bias), m0) >> hs, lo);
+}
+
+__device__ __forceinline__ uint32_t requant4(const uint32_t *acc, int4 bias, const Requant &q) {
+    if (q.hi_path) {
+        const int32_t m0 = (int32_t)q.m0, hs = q.hi_shift, lo = q.lo;
+        return sat_pack4(requant_hi(acc[0], bias.x, m0, hs, lo), requant_hi(acc[1], bias.y, m0, hs, lo),
+                         requant_hi(acc[2], bias.z, m0, hs, lo), requant_hi(acc[3], bias.w, m0, hs, lo));
+    }
+    const int32_t o0 = requant((int32_t)acc[0], bias.x, q), o1 = requant((int32_t)acc[1], bias.y, q);
+    const int32_t o2 = requant((int32_t)acc[2], bias.z, q), o3 = requant((int32_t)acc[3], bias.w, q);
+    return (uint32_t)(o0 & 0xFF) | ((uint32_t)(o1 & 0xFF) << 8) | ((uint32_t)(o2 & 0xFF) << 16) |
+           ((uint32_t)(o3 & 0xFF) << 24);
+}
+
 // ---------------------------------------------------------------------------
 // Exact floor(w * 2^24 / T) for one row with invariant divisor T.
 // Preconditions (guaranteed by build_integer_exp_lut tables, lut[0] = 2^38,

@@ -188,6 +188,10 @@ struct sc_model {
     std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path (box 256 rows)
     std::vector<CUtensorMap> tc_wmaps2;  // weight tensor maps for CTA pairs (box 128 rows)
     sc::Profiler prof;
+    // unit trace of the first SM pair of the fused kernels (sc_trace_enable)
+    unsigned long long *trace_buf = nullptr;
+    unsigned int *trace_count = nullptr;
+    int trace_cap = 0;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
         ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc;

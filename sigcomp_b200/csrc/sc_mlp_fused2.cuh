@@ -35,6 +35,10 @@ struct Fused2Params {
     const int8_t *emb;
     const uint64_t *lut;
     int n_tiles;
+    // optional unit trace of the first CTA pair (null when tracing is off)
+    unsigned long long *trace;        // [2][trace_cap][2]
+    unsigned int *trace_count;        // [2]
+    int trace_cap;
     // compress
     const int32_t *tile_chunk;
     const int32_t *tile_t0;
@@ -58,6 +62,8 @@ namespace {
 
 constexpr int B_HALF = (TN / 2) * KB;          // 16 KB: this CTA's half of a weight K block
 constexpr int EPI_WARPS = 8;                    // epilogue warps per CTA (two per TMEM lane quarter)
+constexpr int BUILD_WARPS = 4;                  // layer-0 builders: warp b owns ring stage b
+constexpr int FUSED2_THREADS = 32 * (2 + EPI_WARPS + BUILD_WARPS);
 constexpr int BIAS_MAX = FMAX_LAYERS * MAX_N;   // int32 entries
 
 template <bool DECODE>
@@ -66,7 +72,8 @@ struct F2Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + B_HALF;                  // 32 KB
     static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 128 KB
     static constexpr int EMB_PAD = 33 * 1024;
-    static constexpr int RING_BYTES = TM * WIN;                           // 8 KB per slot
+    static constexpr int RING_STRIDE = WIN + 1;                           // odd row pitch: no bank conflicts
+    static constexpr int RING_BYTES = TM * RING_STRIDE;                   // per slot
     static constexpr int X_BYTES = DECODE ? EMB_PAD + KT2 * RING_BYTES : 2 * G_BYTES;
     static constexpr int OFF_BIAS = OFF_X + X_BYTES;
     static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
@@ -76,6 +83,101 @@ struct F2Cfg {
     static constexpr int OFF_TMEM = OFF_CNT + 8 * 4;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;
 };
+
+// Trace record of one role event for a unit (first CTA pair only):
+// word 0 = %globaltimer, word 1 = role | event << 4 | L << 8 | nh << 12 | tt << 16 | step << 32.
+// roles: 0 producer, 1 MMA, 2 epilogue (warp 2), 3 layer-0 builders (first warp)
+__device__ __forceinline__ void trace_ev(const Fused2Params &p, int role, int ev, int L, int nh, int tt, int step)
+{
+    if (p.trace == nullptr || blockIdx.x >= 2) return;
+    const unsigned int i = atomicAdd(p.trace_count + blockIdx.x, 1u);
+    if (i >= (unsigned int)p.trace_cap) return;
+    unsigned long long *r = p.trace + ((size_t)blockIdx.x * p.trace_cap + i) * 2;
+    r[0] = globaltimer_ns();
+    r[1] = (unsigned long long)role | ((unsigned long long)ev << 4) | ((unsigned long long)L << 8) |
+           ((unsigned long long)nh << 12) | ((unsigned long long)tt << 16) | ((unsigned long long)step << 32);
+}
+
+// Row frequency statistics (_frequencies, cpu_entropy_coding.py:90-110) from the
+// packed logits in TMEM (64 words from taddr) with the maximum logit m known:
+// row divisor, fix-up amount, first index of the maximum frequency and, for
+// sym >= 0, the exclusive cumulative frequency and frequency of sym.
+__device__ __forceinline__ void row_stats(uint32_t taddr, const uint64_t *lut_s, int m, RowDivisor &d, uint32_t &fix,
+                                          int &amax, int sym, uint32_t &sym_cum, uint32_t &sym_f)
+{
+    uint64_t T = 0;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        uint32_t w[16];
+        tmem_ld16(taddr + g * 16, w);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) T += lut_s[m - pk_get(w[i], b)];
+    }
+    d = make_row_divisor(T);
+    uint32_t total = 0, best = 0, below = 0, fsym = 0;
+    amax = 0;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        uint32_t w[16];
+        tmem_ld16(taddr + g * 16, w);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int v = g * 64 + 4 * i + b;
+                uint32_t f = div_freq(lut_s[m - pk_get(w[i], b)], d);
+                f = f < 1u ? 1u : f;
+                total += f;
+                if (f > best) { best = f; amax = v; }
+                below += v < sym ? f : 0u;
+                fsym = v == sym ? f : fsym;
+            }
+    }
+    fix = total - SC_TOTAL;          // modulo 2^32; subtracting it from f[amax] is exact
+    sym_cum = below - (amax < sym ? fix : 0u);
+    sym_f = fsym - (amax == sym ? fix : 0u);
+}
+
+// The symbol whose cumulative interval holds q: the first v with cum_v + f_v > q.
+// Groups of 64 symbols are scanned only while a lane of the warp is still
+// searching (the TMEM loads are warp-collective).
+__device__ __forceinline__ void row_find(uint32_t taddr, const uint64_t *lut_s, int m, const RowDivisor &d,
+                                         uint32_t fix, int amax, uint32_t q, int &sym, uint32_t &sym_cum,
+                                         uint32_t &sym_f)
+{
+    uint32_t cum = 0;
+    bool found = false;
+    sym = SC_VOCAB - 1;
+    sym_cum = 0;
+    sym_f = 0;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        if (!__any_sync(0xffffffffu, !found)) break;
+        uint32_t w[16];
+        tmem_ld16(taddr + g * 16, w);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int v = g * 64 + 4 * i + b;
+                uint32_t f = div_freq(lut_s[m - pk_get(w[i], b)], d);
+                f = f < 1u ? 1u : f;
+                f -= v == amax ? fix : 0u;
+                if (!found && cum + f > q) {
+                    found = true;
+                    sym = v;
+                    sym_cum = cum;
+                    sym_f = f;
+                }
+                cum += f;
+            }
+    }
+}
 
 // Walk this pair's units in the fixed order both CTAs and every role follow.
 // Pair-tile pt covers tiles 2*pt (rank 0) and 2*pt+1 (rank 1).
@@ -122,7 +224,7 @@ __device__ __forceinline__ void mma_k_block_pair(uint32_t d, uint32_t a_addr, ui
 }
 
 template <bool DECODE>
-__global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused2Params p)
+__global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused2Params p)
 {
     using C = F2Cfg<DECODE>;
     extern __shared__ uint8_t smem_raw[];
@@ -144,7 +246,7 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], DECODE ? 1 + 4 : 1);   // leader producer (+ 2 builder warps x 2 CTAs)
+            mbar_init(&full[s], DECODE ? 1 + 2 : 1);   // leader producer (+ the stage's builder warp in each CTA)
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -181,10 +283,12 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
             uint32_t it = 0;
             for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
                 const int nkb = p.in_dim[L] / KB;
+                trace_ev(p, 0, 0, L, nh, tt, step);
                 if (L >= 1 && nh == 0) {
                     const uint32_t k = (uint32_t)((DECODE ? step : grp) * NL + L - 1);
                     if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return false;
                 }
+                trace_ev(p, 0, 1, L, nh, tt, step);
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return false;
@@ -194,6 +298,7 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                     if (L != 0) tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
+                trace_ev(p, 0, 2, L, nh, tt, step);
                 return true;
             });
         }
@@ -204,7 +309,9 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
             for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
                 const int nkb = p.in_dim[L] / KB;
                 const int ab = uu & 1;
+                trace_ev(p, 1, 0, L, nh, tt, step);
                 if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
+                trace_ev(p, 1, 1, L, nh, tt, step);
                 const int gb = li & 1;
                 if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
                 tc_fence_after();
@@ -212,6 +319,7 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
+                    if (L == 0 && kb < 4) trace_ev(p, 1, 3, L, kb, tt, step);
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
                     const uint32_t a_addr = (!DECODE && L == 0) ? smem_u32(xbuf + gb * G_BYTES) + kb * KB : st;
@@ -219,6 +327,7 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                     mma_commit_pair(&empty[s], 0x3);
                 }
                 mma_commit_pair(&acc_full[ab], 0x3);
+                trace_ev(p, 1, 2, L, nh, tt, step);
                 ++uu;
                 if (!DECODE && L == 0 && nh == p.out_dim[0] / TN - 1) {
                     mma_commit_pair(&g_empty[gb], 0x3);
@@ -236,7 +345,10 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
         uint32_t uu = 0;
         for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
             const int ab = uu & 1;
+            const bool tr = warp == 2 && lane == 0;
+            if (tr) trace_ev(p, 2, 0, L, nh, tt, step);
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[ab], (uu >> 1) & 1))) return false;
+            if (tr) trace_ev(p, 2, 1, L, nh, tt, step);
             ++uu;
             tc_fence_after();
             const uint32_t taddr = tmem_base + ab * TN + ((uint32_t)(q * 32) << 16);
@@ -247,25 +359,21 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
             if (L < NL - 1) {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
 #pragma unroll 1
-                for (int c = half * 4; c < half * 4 + 4; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(taddr + c * 32, v);
+                for (int c = half * 4; c < half * 4 + 4; c += 2) {
+                    uint32_t va[32], vb[32];
+                    tmem_ld32(taddr + c * 32, va);
+                    tmem_ld32(taddr + c * 32 + 32, vb);
                     tmem_ld_wait();
-                    uint32_t packed[8];
+                    const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
+                    uint32_t packed[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        uint32_t w = 0;
+                    for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            const int col = nh * TN + c * 32 + i * 4 + b;
-                            const int32_t o = requant((int32_t)v[i * 4 + b], bias[col], rq);
-                            w |= ((uint32_t)(o & 0xFF)) << (8 * b);
-                        }
-                        packed[i] = w;
-                    }
+                    for (int i = 0; i < 8; ++i) packed[8 + i] = requant4(&vb[4 * i], bv[8 + i], rq);
                     uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
-                    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -275,27 +383,25 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                     __syncwarp();
                     if (lane == 0) counter_add_release(&act_cnt[tt], 1);
                 }
+                if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
                 return true;
             }
             if (half == 0) {
-                // last layer: requantise the 256 logits of this row and keep them packed in
-                // the first 64 columns of the same accumulator (already read)
+                // last layer: requantise the 256 logits of this row, keep them packed in the
+                // first 64 columns of the same accumulator (already read) and track the maximum
+                int mlogit = -128;
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) {
                     uint32_t v[32];
                     tmem_ld32(taddr + c * 32, v);
                     tmem_ld_wait();
+                    const int4 *bv = reinterpret_cast<const int4 *>(bias + c * 32);
                     uint32_t w8[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        uint32_t w = 0;
+                        w8[i] = requant4(&v[4 * i], bv[i], rq);
 #pragma unroll
-                        for (int b = 0; b < 4; ++b) {
-                            const int col = c * 32 + i * 4 + b;
-                            const int32_t o = requant((int32_t)v[i * 4 + b], bias[col], rq);
-                            w |= ((uint32_t)(o & 0xFF)) << (8 * b);
-                        }
-                        w8[i] = w;
+                        for (int b = 0; b < 4; ++b) mlogit = max(mlogit, pk_get(w8[i], b));
                     }
                     tmem_st8(taddr + c * 8, w8);
                 }
@@ -309,10 +415,10 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                     const int64_t begin = p.tok_off[c];
                     const bool valid = real_tile && t0 + r < p.tok_off[c + 1] - begin;
                     const int sym = valid ? p.tokens[begin + t0 + r] : 0;
-                    int m, amax;
+                    int amax;
                     RowDivisor d;
                     uint32_t fix, cum, f;
-                    row_freq_stats(taddr, lut_s, m, d, fix, amax, sym, cum, f);
+                    row_stats(taddr, lut_s, mlogit, d, fix, amax, sym, cum, f);
                     if (valid) p.pairs[begin - p.row_base + t0 + r] = make_uint2(cum, f);
                 } else {
                     const int64_t row = (int64_t)tile * TM + r;
@@ -330,11 +436,11 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                             live = false;
                         }
                     }
-                    int m, amax, sym;
+                    int amax, sym;
                     RowDivisor d;
                     uint32_t fix, cum, f;
-                    row_freq_stats(taddr, lut_s, m, d, fix, amax, -1, cum, f);
-                    row_search(taddr, lut_s, m, d, fix, amax, live ? (uint32_t)qv : 0u, sym, cum, f);
+                    row_stats(taddr, lut_s, mlogit, d, fix, amax, -1, cum, f);
+                    row_find(taddr, lut_s, mlogit, d, fix, amax, live ? (uint32_t)qv : 0u, sym, cum, f);
                     if (live) {
                         s.lower += scale * (uint64_t)cum;
                         s.range = scale * (uint64_t)f;
@@ -348,7 +454,7 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                         p.state[row] = s;
                         p.tokens_out[p.out_off[c] + step] = (uint8_t)sym;
                         uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
-                        ring[r * WIN + (step & (WIN - 1))] = (uint8_t)sym;
+                        ring[r * C::RING_STRIDE + (step & (WIN - 1))] = (uint8_t)sym;
                     }
                 }
             }
@@ -358,44 +464,68 @@ __global__ void __launch_bounds__(384, 1) k_fused2(const __grid_constant__ Fused
                 mbar_arrive_cluster(acc_empty_leader);
                 counter_add_release(&act_cnt[tt], 1);
             }
+            if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
             return true;
         });
     } else if (DECODE) {
-        // ---- warps 10-11: layer-0 activation stages of this CTA's rows from the embedding
-        // table and the window rings; they take part in every ring iteration
-        const int wb = (warp - 10) * 64;
+        // ---- warps 10-13: layer-0 activation stages of this CTA's 128 rows from the
+        // embedding table and the window rings.  Builder warp b owns ring stage b: it
+        // takes part in every iteration of that stage (its arrival is part of the
+        // stage's count) and builds the activation for the layer-0 ones; the four
+        // warps overlap the cluster-scope release of one stage with building others.
+        static_assert(F2Cfg<DECODE>::STAGES == BUILD_WARPS, "one builder warp per ring stage");
+        const int bw = warp - 10;
         const int j = lane & 7, sub = lane >> 3;
         const uint8_t *emb_s = xbuf;
         uint32_t it = 0;
         for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
             const int nkb = p.in_dim[L] / KB;
+            const bool tr = bw == 0 && lane == 0 && L == 0;
+            if (tr) trace_ev(p, 3, 0, L, nh, tt, step);
             if (L == 0 && nh == 0 && step > 0) {
+                // the window ring holds step-1's token once the slot finished its last layer
                 const uint32_t k = (uint32_t)(step * NL - 1);
                 if (!__all_sync(0xffffffffu, counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1)))) return false;
             }
+            if (tr) trace_ev(p, 3, 1, L, nh, tt, step);
             const uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
             for (int kb = 0; kb < nkb; ++kb, ++it) {
                 const int s = it % C::STAGES;
+                if (s != bw) continue;
                 if (!__all_sync(0xffffffffu, mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)))
                     return false;
                 if (L == 0) {
                     uint8_t *a_st = smem + s * C::STAGE_BYTES;
                     const int pos = step - WIN + kb;
-#pragma unroll 4
-                    for (int rr = sub; rr < 64; rr += 4) {
-                        const int rrow = wb + rr;
-                        const int tok = pos < 0 ? SC_SOS : ring[rrow * WIN + (pos & (WIN - 1))];
-                        const int4 v = *reinterpret_cast<const int4 *>(emb_s + tok * EMB_DIM + j * 16);
-                        *reinterpret_cast<int4 *>(a_st + sw128_offset(rrow, j)) = v;
+                    // rows sub, sub+4, ...: per batch all token reads, then all embedding
+                    // reads, then all stores, so the shared-memory latencies overlap
+#pragma unroll 1
+                    for (int b0 = 0; b0 < TM / 4; b0 += 8) {
+                        int tok[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int rrow = sub + 4 * (b0 + i);
+                            tok[i] = pos < 0 ? SC_SOS : ring[rrow * C::RING_STRIDE + (pos & (WIN - 1))];
+                        }
+                        int4 v[8];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i)
+                            v[i] = *reinterpret_cast<const int4 *>(emb_s + tok[i] * EMB_DIM + j * 16);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int rrow = sub + 4 * (b0 + i);
+                            *reinterpret_cast<int4 *>(a_st + sw128_offset(rrow, j)) = v[i];
+                        }
                     }
                     fence_proxy_async_smem();
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(map_to_rank(&full[s], 0));
             }
+            if (tr) trace_ev(p, 3, 2, L, nh, tt, step);
             return true;
         });
-    } else {
+    } else if (warp < 12) {
         // ---- warps 10-11 (compress): sliding embedding buffer of this CTA's tile
         const int tw = threadIdx.x - 320;        // 0..63
         const int j = tw & 7, r0 = tw >> 3;

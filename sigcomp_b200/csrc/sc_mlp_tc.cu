@@ -493,6 +493,12 @@ static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s
     }
     p.emb = m->emb;
     p.lut = m->lut;
+    if (m->trace_cap > 0) {
+        SC_CUDA(cudaMemsetAsync(m->trace_count, 0, 2 * sizeof(unsigned int), s));
+        p.trace = m->trace_buf;
+        p.trace_count = m->trace_count;
+        p.trace_cap = m->trace_cap;
+    }
 }
 
 template <bool DECODE>
@@ -500,7 +506,7 @@ static void launch_pairs(const Fused2Params &p, int grid, cudaStream_t s)
 {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
-    cfg.blockDim = dim3(384);
+    cfg.blockDim = dim3(FUSED2_THREADS);
     cfg.dynamicSmemBytes = F2Cfg<DECODE>::SMEM;
     cfg.stream = s;
     cudaLaunchAttribute attr[1];
