@@ -71,11 +71,14 @@ __global__ void __launch_bounds__(256) k_cdf_select(const int8_t *__restrict__ l
     }
 }
 
-// one thread per chunk: sequential range coding of the chunk's rows, then seal
+// one thread per chunk: sequential range coding of the chunk's rows, then seal.
+// The (cum, freq) pairs are fetched 16 at a time so one memory latency covers
+// 16 symbol steps.
 __global__ void k_encode(const uint2 *__restrict__ pairs, const int64_t *__restrict__ off, int64_t c0,
                          int64_t n, int64_t row_base, uint32_t *__restrict__ stage, int64_t cap,
                          int64_t *__restrict__ nwords, uint8_t *__restrict__ errors)
 {
+    constexpr int PF = 16;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
     const int64_t c = c0 + i;
@@ -84,9 +87,13 @@ __global__ void k_encode(const uint2 *__restrict__ pairs, const int64_t *__restr
     EncState e;
     enc_init(e);
     int err = 0;
-    for (int64_t t = 0; t < len && !err; ++t) {
-        const uint2 p = pairs[begin + t];
-        err = enc_symbol(e, p.x, p.y, out, cap);
+    for (int64_t t0 = 0; t0 < len && !err; t0 += PF) {
+        uint2 pv[PF];
+#pragma unroll
+        for (int k = 0; k < PF; ++k) pv[k] = t0 + k < len ? pairs[begin + t0 + k] : make_uint2(0, 0);
+#pragma unroll
+        for (int k = 0; k < PF; ++k)
+            if (t0 + k < len && !err) err = enc_symbol(e, pv[k].x, pv[k].y, out, cap);
     }
     if (!err) err = enc_seal(e, out, cap);
     nwords[i] = e.pos;
@@ -257,8 +264,13 @@ int compress_device(sc_model *m, const uint8_t *tokens, const int64_t *off_d, co
     int64_t c0 = 0;
     while (c0 < n) {
         // group of chunks whose rows fit one pass (a chunk never exceeds chunk_len rows)
+        // one group for the fused kernels (they need no per-row intermediate beyond the
+        // 8-byte (cum, freq) pair); otherwise groups whose rows fit the activation buffers
+        const bool fused_path = use_tc(m) && fused_supported(m);
+        const int64_t row_limit = fused_path ? ((int64_t)1 << 28) : max_rows;
+        const int64_t chunk_limit = fused_path ? ((int64_t)1 << 20) : n;
         int64_t c1 = c0;
-        while (c1 < n && (c1 == c0 || off_h[c1 + 1] - off_h[c0] <= max_rows)) ++c1;
+        while (c1 < n && (c1 == c0 || (off_h[c1 + 1] - off_h[c0] <= row_limit && c1 - c0 < chunk_limit))) ++c1;
         const int64_t gn = c1 - c0;
         const int64_t row_base = off_h[c0], rows = off_h[c1] - off_h[c0];
         int64_t max_len = 0;

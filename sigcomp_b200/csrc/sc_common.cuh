@@ -71,6 +71,12 @@ __device__ __forceinline__ int32_t requant_hi(uint32_t acc, int32_t bias, int32_
     return max(__mulhi((int32_t)(acc + (uint32_t)bias), m0) >> hs, lo);
 }
 
+// requant4 with the fast-path parameters in registers (M0 < 2^31, shift >= 32)
+__device__ __forceinline__ uint32_t requant4_hi(const uint32_t *acc, int4 bias, int32_t m0, int32_t hs, int32_t lo) {
+    return sat_pack4(requant_hi(acc[0], bias.x, m0, hs, lo), requant_hi(acc[1], bias.y, m0, hs, lo),
+                     requant_hi(acc[2], bias.z, m0, hs, lo), requant_hi(acc[3], bias.w, m0, hs, lo));
+}
+
 __device__ __forceinline__ uint32_t requant4(const uint32_t *acc, int4 bias, const Requant &q) {
     if (q.hi_path) {
         const int32_t m0 = (int32_t)q.m0, hs = q.hi_shift, lo = q.lo;

@@ -353,6 +353,9 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             tc_fence_after();
             const uint32_t taddr = tmem_base + ab * TN + ((uint32_t)(q * 32) << 16);
             const Requant rq = p.rq[L];
+            // fast-path parameters as scalars (uniform per unit)
+            const bool rq_fast = rq.hi_path != 0;
+            const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_lo = rq.lo;
             const int32_t *bias = bias_s + L * MAX_N;
             const uint32_t acc_empty_leader = map_to_rank(&acc_empty[ab], 0);
             const int tile = 2 * pt + (int)rank;
@@ -366,10 +369,18 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                     tmem_ld_wait();
                     const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
                     uint32_t packed[16];
+                    if (rq_fast) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
+                        for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_lo);
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) packed[8 + i] = requant4(&vb[4 * i], bv[8 + i], rq);
+                        for (int i = 0; i < 8; ++i)
+                            packed[8 + i] = requant4_hi(&vb[4 * i], bv[8 + i], rq_m0, rq_hs, rq_lo);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) packed[8 + i] = requant4(&vb[4 * i], bv[8 + i], rq);
+                    }
                     uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
 #pragma unroll
                     for (int i = 0; i < 4; ++i)
@@ -377,7 +388,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                 }
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(acc_empty_leader);
+                if (lane == 0) mbar_arrive_cluster_relaxed(acc_empty_leader);
                 if (nh == p.out_dim[L] / TN - 1) {
                     fence_proxy_async_global();
                     __syncwarp();
@@ -399,7 +410,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                     uint32_t w8[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        w8[i] = requant4(&v[4 * i], bv[i], rq);
+                        w8[i] = rq_fast ? requant4_hi(&v[4 * i], bv[i], rq_m0, rq_hs, rq_lo) : requant4(&v[4 * i], bv[i], rq);
 #pragma unroll
                         for (int b = 0; b < 4; ++b) mlogit = max(mlogit, pk_get(w8[i], b));
                     }
@@ -461,7 +472,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive_cluster(acc_empty_leader);
+                mbar_arrive_cluster_relaxed(acc_empty_leader);
                 counter_add_release(&act_cnt[tt], 1);
             }
             if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
