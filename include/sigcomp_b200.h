@@ -135,6 +135,29 @@ SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t
                          void *stream);
 
 /*
+ * sc_mlp_logits_device without any device allocation.  No counterpart in the
+ * reference: it exists for callers that cannot call cudaMalloc, such as a host
+ * framework that has reserved the GPU's memory for its own pool, or a
+ * latency-critical caller that cannot accept the device-wide synchronisation
+ * of cudaMalloc/cudaFree.  Same arguments and the same logits as
+ * sc_mlp_logits_device (computed by the CUDA-core layer kernels).
+ *
+ * Its intermediate activations live in a fixed device array of
+ * 2 x SC_NOALLOC_MAX_ROWS x SC_NOALLOC_MAX_WIDTH bytes (4 MiB), held on every
+ * GPU that loads the library until the process exits.  rows above
+ * SC_NOALLOC_MAX_ROWS return SC_ERR_INVALID_ARGUMENT; a model with a hidden
+ * layer wider than SC_NOALLOC_MAX_WIDTH returns SC_ERR_UNSUPPORTED.
+ * The first call on a device looks up the array's device address (a one-time
+ * set-up); make that first call before any stream capture.  All calls share
+ * the array: calls whose work overlaps on the GPU (other streams, threads or
+ * models on the same device) race and must be serialised by the caller.
+ */
+#define SC_NOALLOC_MAX_ROWS  4096
+#define SC_NOALLOC_MAX_WIDTH 512
+SC_API int sc_mlp_logits_device_noalloc(sc_model *model, const int16_t *windows, int64_t rows,
+                                        int8_t *logits, void *stream);
+
+/*
  * Per-launch CUDA-event timing (no counterpart in the reference; instrumentation
  * for the benchmark's roofline).  sc_profile_enable(m, 1) resets the counters and
  * starts recording an event pair around every launch on its own stream;

@@ -22,7 +22,7 @@ EXPORTS = (
     "sc_version", "sc_last_error", "sc_kernel_launches", "sc_model_create", "sc_model_destroy",
     "sc_model_set_mlp_path", "sc_compress_chunks", "sc_compress_chunks_device", "sc_decompress_chunks",
     "sc_decompress_chunks_device", "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read",
-    "sc_trace_enable", "sc_trace_read",
+    "sc_trace_enable", "sc_trace_read", "sc_mlp_logits_device_noalloc",
 )
 
 KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step")
@@ -65,7 +65,8 @@ def load():
         getattr(L, name)
     for name in ("sc_model_create", "sc_model_destroy", "sc_model_set_mlp_path", "sc_compress_chunks",
                  "sc_compress_chunks_device", "sc_decompress_chunks", "sc_decompress_chunks_device",
-                 "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read"):
+                 "sc_mlp_logits_device", "sc_mlp_logits_device_noalloc", "sc_profile_enable",
+                 "sc_profile_read"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L

@@ -4,7 +4,10 @@
 // epilogue of _requantize (sigcomp/cpu_int_kernels.py:5-14).  Layer 0 gathers
 // its input rows from the embedding table through the context windows,
 // x[row, p*E + c] = E_q[window[row, p], c] (sigcomp/cpu_int_kernels.py:107-121).
+#include <mutex>
+
 #include "sc_internal.h"
+#include "../../include/sigcomp_b200.h"
 
 namespace sc {
 namespace {
@@ -103,3 +106,111 @@ void mlp_simple(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logit
 }
 
 }  // namespace sc
+
+// ---------------------------------------------------------------------------
+// Allocation-free MLP logits (sc_mlp_logits_device_noalloc).
+//
+// Some callers cannot call cudaMalloc: a host framework that has reserved the
+// GPU's memory for its own pool (a serving engine's caching allocator) makes a
+// library's own cudaMalloc fail or fragment that pool, and a latency-critical
+// caller cannot accept the implicit device synchronisation of cudaMalloc and
+// cudaFree.  sc_mlp_logits_device grows per-model activation buffers on first
+// use; this variant runs the same CUDA-core layer kernels with the two
+// ping-pong activation buffers in a fixed, file-scope device array instead.
+//
+// The array is loaded with the library and held on every GPU that loads it
+// until the process exits.  All calls share it and it keeps the last call's
+// contents; every layer overwrites all the rows it later reads, so nothing in
+// it needs clearing.  Calls whose work overlaps on the GPU (two streams, two
+// threads, two models on one device) race on the array.
+// ---------------------------------------------------------------------------
+namespace sc {
+namespace {
+
+constexpr int64_t kNoAllocMaxRows = SC_NOALLOC_MAX_ROWS;
+constexpr int kNoAllocMaxWidth = SC_NOALLOC_MAX_WIDTH;
+constexpr size_t kNoAllocBufBytes = (size_t)kNoAllocMaxRows * kNoAllocMaxWidth;
+
+static __device__ __align__(256) int8_t g_noalloc_scratch[2 * kNoAllocBufBytes];
+
+// Device address of g_noalloc_scratch per device ordinal.  In host code the
+// array's name is a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress, called once per device with that device current.
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+int8_t *g_noalloc_ptr[kMaxDevices] = {};
+
+int8_t *noalloc_scratch(int device)
+{
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_ptr[device]) {
+        void *p = nullptr;
+        SC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_ptr[device] = (int8_t *)p;
+    }
+    return g_noalloc_ptr[device];
+}
+
+}  // namespace
+
+}  // namespace sc
+
+extern "C" SC_API int sc_mlp_logits_device_noalloc(sc_model *m, const int16_t *windows, int64_t rows,
+                                                   int8_t *logits, void *stream)
+{
+    using namespace sc;
+    set_error("%s", "");
+    if (!m || rows < 0 || (rows > 0 && (!windows || !logits))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    if (rows > kNoAllocMaxRows) {
+        set_error("sc_mlp_logits_device_noalloc: %lld rows exceed its fixed scratch limit of %lld rows "
+                  "(split the batch, or use sc_mlp_logits_device)",
+                  (long long)rows, (long long)kNoAllocMaxRows);
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    for (int l = 0; l + 1 < m->num_layers; ++l)
+        if (m->layers[l].out_dim > kNoAllocMaxWidth) {
+            set_error("sc_mlp_logits_device_noalloc: layer %d is %d wide, above the scratch width of %d", l,
+                      m->layers[l].out_dim, kNoAllocMaxWidth);
+            return SC_ERR_UNSUPPORTED;
+        }
+    if (m->device < 0 || m->device >= kMaxDevices) {
+        set_error("sc_mlp_logits_device_noalloc: device %d out of range", m->device);
+        return SC_ERR_UNSUPPORTED;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    if (prev != m->device) cudaSetDevice(m->device);
+    int rc = SC_OK;
+    try {
+        if (rows > 0) {
+            int8_t *base = noalloc_scratch(m->device);
+            int8_t *bufs[2] = {base, base + kNoAllocBufBytes};
+            const int8_t *x = nullptr;
+            for (int l = 0; l < m->num_layers; ++l) {
+                const LayerDev &L = m->layers[l];
+                int8_t *y = (l == m->num_layers - 1) ? logits : bufs[l & 1];
+                dim3 grid((L.out_dim + BN - 1) / BN, (unsigned)((rows + BM - 1) / BM));
+                if (l == 0)
+                    k_linear_dp4a<true><<<grid, 256, 0, s>>>(nullptr, windows, m->emb, m->emb_dim, m->window,
+                                                             L.w, L.bias, L.rq, y, rows, L.out_dim, L.in_dim);
+                else
+                    k_linear_dp4a<false><<<grid, 256, 0, s>>>(x, nullptr, nullptr, 0, 0, L.w, L.bias, L.rq, y,
+                                                              rows, L.out_dim, L.in_dim);
+                SC_LAUNCH_CHECK();
+                count_launch();
+                x = y;
+            }
+        }
+        SC_CUDA(cudaStreamSynchronize(s));
+    } catch (const CudaError &e) {
+        set_error("CUDA error %s (%s) in %s", cudaGetErrorName(e.code), cudaGetErrorString(e.code),
+                  e.where.c_str());
+        rc = SC_ERR_CUDA;
+    }
+    if (prev >= 0 && prev != m->device) cudaSetDevice(prev);
+    return rc;
+}
