@@ -14,8 +14,11 @@ lays out the archive.
              (device entry points sc_compress_chunks_device / sc_decompress_chunks_device)
   e2e        the same through the host entry points (sc_compress_chunks /
              sc_decompress_chunks) from pinned host memory, copies timed
-  roofline   the dominant kernel (MLP layer 0, tcgen05 int8 GEMM) against the
-             int8 tensor throughput measured in the same run with torch._int_mm
+  roofline   the dominant kernel (the persistent autoregressive decoder, all nine
+             tcgen05 int8 layers + frequency search + range decoding in one launch)
+             against the int8 tensor throughput measured in the same run with
+             torch._int_mm; roofline_compress does the same for the fused compress
+             kernel
   cpu_baseline  the CPU port of the reference codec (int_mm + C coder, oracle/)
              on a bounded sample, rank 0 at N=1
 
@@ -39,15 +42,18 @@ sys.path.insert(0, str(REPO))
 METRIC = "compress & decompress Msamples/s at 1/2/4/8 B200; bits/sample (bit-exact)"
 UNIT = "Msamples/s"
 CHUNK_LEN = 2048
+# int8 MLP work per coded token: 2 x (8192*512 + 7*512*512 + 512*256) multiply-adds
+OPS_PER_TOKEN = 2 * (8192 * 512 + 7 * 512 * 512 + 512 * 256)
 
 
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--reads", type=int, default=4000, help="reads per GPU per step")
+    ap.add_argument("--reads", type=int, default=20000,
+                    help="reads per GPU per step (configuration 2 is 20,000 reads)")
     ap.add_argument("--cpu-reads", type=int, default=12, help="reads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -344,32 +350,40 @@ def main():
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
                "entry_points": "sc_compress_chunks + sc_decompress_chunks (host buffers, pinned)"}
 
-    # ---- roofline of the dominant kernel ---------------------------------------
-    roofline = None
+    # ---- roofline of the fused kernels ------------------------------------------
+    roofline = roofline_c = None
     if rank == 0:
-        l0_ms, l0_n, l0_rows = prof["layer0"]
         peak = int8_peak_tops()
-        ops_per_row = 2 * 512 * 8192
-        achieved = l0_rows * ops_per_row / (l0_ms * 1e-3) / 1e12 if l0_ms > 0 else 0.0
         all_ms = sum(v[0] for v in prof.values())
-        traffic = None
-        tf = REPO / "profiles" / "layer0_traffic.json"
-        if tf.exists():
-            t = json.loads(tf.read_text())
-            traffic = round(t["dram_bytes_per_row"] * (l0_rows / max(l0_n, 1)))
-        roofline = {
-            "kernel": "k_linear_tc<gather> (MLP layer 0, tcgen05 int8, 128x256 tiles)",
-            "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOP/s (int8)",
-            "frac": round(achieved / peak, 4) if peak else None, "traffic": traffic,
-            "peak_source": "torch._int_mm int8 8192^3 best of 10, measured in this run (MEASURED_PEAKS.json has "
-                           "no int8 figure); datasheet dense int8 is 4500 TOP/s",
-            "frac_of_datasheet": round(achieved / 4500.0, 4),
-            "ops_per_launch": int(ops_per_row * l0_rows / max(l0_n, 1)), "launches": l0_n,
-            "avg_launch_ms": round(l0_ms / max(l0_n, 1), 4),
-            "share_of_gpu_time": round(l0_ms / all_ms, 4) if all_ms else None,
-            "kernel_ms": {k: round(v[0], 2) for k, v in prof.items()},
-            "kernel_launches": {k: v[1] for k, v in prof.items()},
-        }
+        traffic_file = REPO / "profiles" / "fused_traffic.json"
+        traffic_per_token = json.loads(traffic_file.read_text()) if traffic_file.exists() else {}
+
+        def fused_roofline(kind, name):
+            ms, n, toks = prof[kind]
+            if ms <= 0 or n == 0:
+                return None
+            achieved = toks * OPS_PER_TOKEN / (ms * 1e-3) / 1e12
+            tpt = traffic_per_token.get(kind)
+            return {
+                "kernel": name, "bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                "unit": "TOP/s (int8)", "frac": round(achieved / peak, 4) if peak else None,
+                "traffic": round(tpt * toks / n) if tpt else None,
+                "peak_source": "torch._int_mm int8 8192^3 best of 10, measured in this run (MEASURED_PEAKS.json "
+                               "has no int8 figure); datasheet dense int8 is 4500 TOP/s",
+                "frac_of_datasheet": round(achieved / 4500.0, 4),
+                "ops_per_token": OPS_PER_TOKEN, "tokens_per_launch": int(toks / n),
+                "ops_per_launch": int(OPS_PER_TOKEN * toks / n), "launches": n,
+                "avg_launch_ms": round(ms / n, 3),
+                "share_of_gpu_time": round(ms / all_ms, 4) if all_ms else None,
+            }
+
+        roofline = fused_roofline("fused_decode", "k_fused2<1>: persistent autoregressive decoder on SM pairs "
+                                                 "(9 tcgen05 int8 layers + frequency search + range decode)")
+        roofline_c = fused_roofline("fused_compress", "k_fused2<0>: fused compress on SM pairs (9 tcgen05 int8 layers "
+                                              "+ (cum, freq) selection)")
+        if roofline is not None:
+            roofline["kernel_ms"] = {k: round(v[0], 2) for k, v in prof.items()}
+            roofline["kernel_launches"] = {k: v[1] for k, v in prof.items()}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -397,7 +411,8 @@ def main():
             "bits_per_small_token": round(8 * total_stream / total_tokens, 4),
             "bit_exact_round_trip": all_ok,
             "gpu_launches": int(launches),
-            "clocks": clk, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e,
+            "clocks": clk, "roofline": roofline, "roofline_compress": roofline_c, "cpu_baseline": cpu,
+            "e2e": e2e,
         }
         print(json.dumps(line), flush=True)
     codec.close()

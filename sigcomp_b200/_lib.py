@@ -25,7 +25,8 @@ EXPORTS = (
     "sc_trace_enable", "sc_trace_read", "sc_mlp_logits_device_noalloc",
 )
 
-KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step")
+KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step",
+                "fused_compress", "fused_decode")
 
 _lib = None
 

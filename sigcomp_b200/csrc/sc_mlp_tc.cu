@@ -524,7 +524,7 @@ void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_
                     cudaStream_t s)
 {
     if (n_tiles <= 0) return;
-    ProfScope ps(m->prof, KK_LAYER0, s, rows);
+    ProfScope ps(m->prof, KK_FUSED_COMPRESS, s, rows);
     if (use_pairs(m)) {
         const int64_t n_pt = (n_tiles + 1) / 2;
         const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);
@@ -561,7 +561,7 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
 {
     if (n_rows <= 0) return;
     const int64_t n_tiles = (n_rows + TM - 1) / TM;
-    ProfScope ps(m->prof, KK_DECODE, s, work_rows);
+    ProfScope ps(m->prof, KK_FUSED_DECODE, s, work_rows);
     if (use_pairs(m)) {
         const int64_t n_pt = (n_tiles + 1) / 2;
         const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);

@@ -17,6 +17,8 @@ Fixtures written:
   coder.npz        - logits + symbols -> range-coded streams (python and numba coders)
   streams_<model>.npz - synthetic reads -> tokens -> reference compress_chunks streams
   signal.npz       - reference _split_signal / lossy transform outputs
+  sharding.json    - sample counts -> read ranges of the reference multi-GPU partition
+                     (sigcomp/read_assignment.py); `--only sharding` rewrites just this file
 """
 
 import argparse
@@ -100,11 +102,45 @@ def _encode_reference(ce, lut, logits, symbols, backend):
     return enc.get_compressed()[0], saw_inversion
 
 
+def _sharding_cases(path):
+    """Read ranges of sample_balanced_ranges for edge cases and synthetic read sets."""
+    sys.path.insert(0, str(path))
+    from sigcomp.read_assignment import sample_balanced_ranges
+    rng = np.random.default_rng(7)
+    inputs = [
+        ([], 4), ([5], 1), ([5], 8), ([0, 0, 0, 0, 0], 2), ([0, 0, 0, 0, 0, 0, 0], 3),
+        ([1, 1, 1, 1], 4), ([10, 1, 1, 1], 2), ([1, 1, 1, 10], 2), ([3, 3], 2), ([4, 2, 2], 2),
+        ([1000000, 1, 1, 1, 1, 1], 3), ([2 ** 62, 2 ** 62 - 1, 1, 7, 2 ** 62], 3), ([0, 9, 0, 9, 0], 4),
+    ]
+    for workers in (1, 2, 3, 4, 7, 8):
+        counts = np.clip(np.rint(rng.lognormal(np.log(30000), 0.8, size=500)), 2000, 1000000)
+        inputs.append(([int(c) for c in counts], workers))
+        counts = rng.integers(0, 5, size=37)
+        inputs.append(([int(c) for c in counts], workers))
+    cases = []
+    for counts, workers in inputs:
+        ranges = sample_balanced_ranges(counts, workers)
+        cases.append({"counts": counts, "workers": workers,
+                      "ranges": [[r.start, r.stop, r.num_samples] for r in ranges]})
+    errors = []
+    for counts, workers in (([1, 2], 0), ([1, -1], 2), ([2 ** 64 - 1, 1], 2)):
+        try:
+            sample_balanced_ranges(counts, workers)
+            errors.append({"counts": counts, "workers": workers, "error": None})
+        except ValueError as e:
+            errors.append({"counts": counts, "workers": workers, "error": str(e)})
+    (HERE / "sharding.json").write_text(json.dumps({"cases": cases, "errors": errors}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", "/root/reference"))
+    ap.add_argument("--only", choices=["sharding"], default=None)
     args = ap.parse_args()
     os.environ.setdefault("NUMBA_CACHE_DIR", "/tmp/nbcache")
+    _sharding_cases(Path(args.reference))
+    if args.only == "sharding":
+        return
     cc, ce, ci, sm = _import_reference(Path(args.reference))
     sys.path.insert(0, str(REPO))
     from sigcomp_b200 import synthetic
