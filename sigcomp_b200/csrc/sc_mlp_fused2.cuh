@@ -338,15 +338,43 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
         }
     } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
         // ---- epilogue warps: TMEM lane quarter q; hidden layers split the 256 columns of
-        // a unit between the two warps of a quarter, the last layer runs on the first one
+        // a unit between the two warps of a quarter.  The last layer of a unit runs on
+        // one warp of the quarter, the two warps taking turns: by tile slot for decoding
+        // (so a row's coder state always stays with the warp that wrote it), by unit for
+        // compression.
         const int q = warp & 3;
         const int half = (warp - 2) >> 2;
         const int r = q * 32 + lane;
-        uint32_t uu = 0;
+        uint32_t uu = 0, lu = 0;
         for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
             const int ab = uu & 1;
             const bool tr = warp == 2 && lane == 0;
             if (tr) trace_ev(p, 2, 0, L, nh, tt, step);
+            bool mine = false;
+            if (L == NL - 1) {
+                mine = DECODE ? (((tt + grp) & 1) == half) : ((int)(lu & 1) == half);
+                ++lu;
+            }
+            // decoding: this row's coder state and quotient, fetched before the logits are ready
+            int64_t drow = 0, dc = 0;
+            bool dlive = false;
+            DecState ds{};
+            uint64_t dscale = 0, dq = 0;
+            if (DECODE && mine) {
+                drow = (int64_t)(2 * pt + (int)rank) * TM + r;
+                dlive = drow < p.n_rows;
+                dc = dlive ? p.order[drow] : 0;
+                dlive = dlive && step < p.lengths[dc] && !p.errors[dc];
+                if (dlive) {
+                    ds = p.state[drow];
+                    dscale = ds.range >> SC_PRECISION;
+                    dq = dscale ? (ds.point - ds.lower) / dscale : ~0ull;
+                    if (dq >= (uint64_t)SC_TOTAL) {      // invalid stream (cpu_entropy_coding.py:244-248)
+                        p.errors[dc] = 1;
+                        dlive = false;
+                    }
+                }
+            }
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[ab], (uu >> 1) & 1))) return false;
             if (tr) trace_ev(p, 2, 1, L, nh, tt, step);
             ++uu;
@@ -397,7 +425,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                 if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
                 return true;
             }
-            if (half == 0) {
+            if (mine) {
                 // last layer: requantise the 256 logits of this row, keep them packed in the
                 // first 64 columns of the same accumulator (already read) and track the maximum
                 int mlogit = -128;
@@ -432,29 +460,15 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                     row_stats(taddr, lut_s, mlogit, d, fix, amax, sym, cum, f);
                     if (valid) p.pairs[begin - p.row_base + t0 + r] = make_uint2(cum, f);
                 } else {
-                    const int64_t row = (int64_t)tile * TM + r;
-                    bool live = row < p.n_rows;
-                    const int64_t c = live ? p.order[row] : 0;
-                    live = live && step < p.lengths[c] && !p.errors[c];
-                    DecState s{};
-                    uint64_t scale = 0, qv = 0;
-                    if (live) {
-                        s = p.state[row];
-                        scale = s.range >> SC_PRECISION;
-                        qv = scale ? (s.point - s.lower) / scale : ~0ull;
-                        if (qv >= (uint64_t)SC_TOTAL) {      // invalid stream (cpu_entropy_coding.py:244-248)
-                            p.errors[c] = 1;
-                            live = false;
-                        }
-                    }
                     int amax, sym;
                     RowDivisor d;
                     uint32_t fix, cum, f;
                     row_stats(taddr, lut_s, mlogit, d, fix, amax, -1, cum, f);
-                    row_find(taddr, lut_s, mlogit, d, fix, amax, live ? (uint32_t)qv : 0u, sym, cum, f);
-                    if (live) {
-                        s.lower += scale * (uint64_t)cum;
-                        s.range = scale * (uint64_t)f;
+                    row_find(taddr, lut_s, mlogit, d, fix, amax, dlive ? (uint32_t)dq : 0u, sym, cum, f);
+                    if (dlive) {
+                        DecState s = ds;
+                        s.lower += dscale * (uint64_t)cum;
+                        s.range = dscale * (uint64_t)f;
                         if (s.range < (1ull << 32)) {
                             s.lower <<= 32;
                             s.range <<= 32;
@@ -462,8 +476,8 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                             if (s.read_pos < s.end_pos) s.point |= p.words[s.read_pos];
                             s.read_pos += 1;
                         }
-                        p.state[row] = s;
-                        p.tokens_out[p.out_off[c] + step] = (uint8_t)sym;
+                        p.state[drow] = s;
+                        p.tokens_out[p.out_off[dc] + step] = (uint8_t)sym;
                         uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
                         ring[r * C::RING_STRIDE + (step & (WIN - 1))] = (uint8_t)sym;
                     }
