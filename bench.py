@@ -57,10 +57,13 @@ def parse_args():
     ap.add_argument("--cpu-reads", type=int, default=12, help="reads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
+                    help="tokens per chunk (2048 in every configuration; smaller values give short "
+                         "decoder launches for profiling)")
     return ap.parse_args()
 
 
-def make_batch(rank, n_reads):
+def make_batch(rank, n_reads, chunk_len=CHUNK_LEN):
     """Token chunks of one rank's batch: (samples, tokens, offsets, per-read token counts)."""
     from sigcomp_b200 import signal, synthetic
     reads = synthetic.make_reads("r10_lognormal", seed=1000 + rank, count=n_reads)
@@ -68,7 +71,7 @@ def make_batch(rank, n_reads):
     toks = [signal.split_signal(r)[1] for r in reads]
     lengths = []
     for t in toks:
-        lengths += [min(CHUNK_LEN, len(t) - i) for i in range(0, len(t), CHUNK_LEN)]
+        lengths += [min(chunk_len, len(t) - i) for i in range(0, len(t), chunk_len)]
     offsets = np.zeros(len(lengths) + 1, dtype=np.int64)
     np.cumsum(lengths, out=offsets[1:])
     tokens = np.concatenate(toks).astype(np.uint8)
@@ -214,11 +217,11 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    samples, tokens, offsets, read_tokens = make_batch(rank, args.reads)
+    samples, tokens, offsets, read_tokens = make_batch(rank, args.reads, args.chunk_len)
     n_chunks = len(offsets) - 1
     n_tok = int(offsets[-1])
     lengths = np.diff(offsets)
-    codec = B200Compression(chunk_len=CHUNK_LEN, gpu=local, model=load_model(name="lossless"))
+    codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name="lossless"))
     L = codec._lib
     h = codec.handle
     vp = ctypes.c_void_p
@@ -401,7 +404,8 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": "r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, "
-                                   "levels N(500,60), dwell 12, noise 12), lossless model, chunk_len 2048",
+                                   "levels N(500,60), dwell 12, noise 12), lossless model, "
+                                   f"chunk_len {args.chunk_len}",
                        "reads_per_gpu": args.reads, "samples_per_gpu": samples, "tokens_per_gpu": n_tok,
                        "chunks_per_gpu": n_chunks, "parallelism": f"reads sharded over {world} GPU(s)",
                        "l2": "inputs larger than L2 (tokens per GPU > 126 MB; activations stream through HBM)"},
