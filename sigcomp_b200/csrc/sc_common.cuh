@@ -28,6 +28,7 @@ struct Requant {
     int32_t lo;      // 0 with ReLU, -128 without
     int32_t hi_path; // 1: m0 < 2^31 and shift >= 32 -> 32-bit mulhi form
     int32_t hi_shift;
+    int32_t one;     // 1 (a run-time operand of the fast path's multiply-add)
 };
 
 __host__ __device__ inline Requant make_requant(int64_t m0, int32_t shift, int32_t relu) {
@@ -37,6 +38,7 @@ __host__ __device__ inline Requant make_requant(int64_t m0, int32_t shift, int32
     r.lo = relu ? 0 : -128;
     r.hi_path = (m0 < (1ll << 31) && shift >= 32) ? 1 : 0;
     r.hi_shift = shift - 32;
+    r.one = 1;
     return r;
 }
 
@@ -71,10 +73,21 @@ __device__ __forceinline__ int32_t requant_hi(uint32_t acc, int32_t bias, int32_
     return max(__mulhi((int32_t)(acc + (uint32_t)bias), m0) >> hs, lo);
 }
 
-// requant4 with the fast-path parameters in registers (M0 < 2^31, shift >= 32)
-__device__ __forceinline__ uint32_t requant4_hi(const uint32_t *acc, int4 bias, int32_t m0, int32_t hs, int32_t lo) {
-    return sat_pack4(requant_hi(acc[0], bias.x, m0, hs, lo), requant_hi(acc[1], bias.y, m0, hs, lo),
-                     requant_hi(acc[2], bias.z, m0, hs, lo), requant_hi(acc[3], bias.w, m0, hs, lo));
+// requant4 with the fast-path parameters in registers (M0 < 2^31, shift >= 32),
+// arranged to spread the work over the integer pipes: the bias is added by a
+// multiply-add (`one` is 1 at run time), cvt.pack.sat clamps to [-128, 127],
+// and the ReLU lower bound is applied to the four packed bytes at once
+// (prmt replicates each byte's sign; relu_mask is all ones with ReLU, else 0).
+__device__ __forceinline__ uint32_t requant4_hi(const uint32_t *acc, int4 bias, int32_t m0, int32_t hs,
+                                                uint32_t relu_mask, int32_t one) {
+    const int32_t v0 = __mulhi((int32_t)(acc[0] * (uint32_t)one + (uint32_t)bias.x), m0) >> hs;
+    const int32_t v1 = __mulhi((int32_t)(acc[1] * (uint32_t)one + (uint32_t)bias.y), m0) >> hs;
+    const int32_t v2 = __mulhi((int32_t)(acc[2] * (uint32_t)one + (uint32_t)bias.z), m0) >> hs;
+    const int32_t v3 = __mulhi((int32_t)(acc[3] * (uint32_t)one + (uint32_t)bias.w), m0) >> hs;
+    const uint32_t d = sat_pack4(v0, v1, v2, v3);
+    uint32_t sgn;
+    asm("prmt.b32 %0, %1, %1, 0xBA98;" : "=r"(sgn) : "r"(d));
+    return d & ~(sgn & relu_mask);
 }
 
 __device__ __forceinline__ uint32_t requant4(const uint32_t *acc, int4 bias, const Requant &q) {

@@ -383,7 +383,8 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             const Requant rq = p.rq[L];
             // fast-path parameters as scalars (uniform per unit)
             const bool rq_fast = rq.hi_path != 0;
-            const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_lo = rq.lo;
+            const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_one = rq.one;
+            const uint32_t rq_relu = rq.lo == 0 ? 0xFFFFFFFFu : 0u;
             const int32_t *bias = bias_s + L * MAX_N;
             const uint32_t acc_empty_leader = map_to_rank(&acc_empty[ab], 0);
             const int tile = 2 * pt + (int)rank;
@@ -399,10 +400,10 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                     uint32_t packed[16];
                     if (rq_fast) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_lo);
+                        for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one);
 #pragma unroll
                         for (int i = 0; i < 8; ++i)
-                            packed[8 + i] = requant4_hi(&vb[4 * i], bv[8 + i], rq_m0, rq_hs, rq_lo);
+                            packed[8 + i] = requant4_hi(&vb[4 * i], bv[8 + i], rq_m0, rq_hs, rq_relu, rq_one);
                     } else {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
@@ -438,7 +439,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                     uint32_t w8[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        w8[i] = rq_fast ? requant4_hi(&v[4 * i], bv[i], rq_m0, rq_hs, rq_lo) : requant4(&v[4 * i], bv[i], rq);
+                        w8[i] = rq_fast ? requant4_hi(&v[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one) : requant4(&v[4 * i], bv[i], rq);
 #pragma unroll
                         for (int b = 0; b < 4; ++b) mlogit = max(mlogit, pk_get(w8[i], b));
                     }
