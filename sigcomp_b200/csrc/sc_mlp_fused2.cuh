@@ -14,8 +14,13 @@
 //     `empty`, `acc_full` and `g_empty` barriers of both CTAs;
 //   - each CTA's epilogue warps read their own 128 TMEM lanes and arrive on the
 //     leader's `acc_empty` (remote arrive for the peer);
-//   - layer-0 builders (decode: activation stages, compress: sliding buffers)
-//     work on their own CTA's rows and arrive on the leader's barriers.
+//   - compress: layer-0 builders fill sliding embedding buffers of their own
+//     CTA's rows and arrive on the leader's barriers;
+//   - decode: layer 0 reads its operand by TMA from a per-tile embedding ring
+//     in global memory (the embedding rows of the last 64 tokens of every row,
+//     one 128-row x 128-byte block per window position); the last-layer
+//     epilogue appends each decoded token's embedding row, so a step writes
+//     one block per tile instead of building all 64.
 // No TMA load uses cluster multicast.
 #pragma once
 
@@ -47,6 +52,9 @@ struct Fused2Params {
     int64_t row_base;
     uint2 *pairs;
     // decode
+    CUtensorMap ering;                // embedding ring, box 128 rows x 128 B
+    int8_t *ering_ptr;                // [grid][KT2][WIN][TM][128], then the start-of-sequence block
+    int64_t ering_sos_row;            // first row of the start-of-sequence block
     const int64_t *order;
     int64_t n_rows;
     const int32_t *tile_maxlen;
@@ -62,19 +70,17 @@ namespace {
 
 constexpr int B_HALF = (TN / 2) * KB;          // 16 KB: this CTA's half of a weight K block
 constexpr int EPI_WARPS = 8;                    // epilogue warps per CTA (two per TMEM lane quarter)
-constexpr int BUILD_WARPS = 4;                  // layer-0 builders: warp b owns ring stage b
+constexpr int BUILD_WARPS = 4;                  // compress: warps 10-11 fill the sliding buffers
 constexpr int FUSED2_THREADS = 32 * (2 + EPI_WARPS + BUILD_WARPS);
 constexpr int BIAS_MAX = FMAX_LAYERS * MAX_N;   // int32 entries
 
 template <bool DECODE>
 struct F2Cfg {
-    static constexpr int STAGES = 4;
+    static constexpr int STAGES = DECODE ? 5 : 4;
     static constexpr int STAGE_BYTES = A_BYTES + B_HALF;                  // 32 KB
-    static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 128 KB
-    static constexpr int EMB_PAD = 33 * 1024;
-    static constexpr int RING_STRIDE = WIN + 1;                           // odd row pitch: no bank conflicts
-    static constexpr int RING_BYTES = TM * RING_STRIDE;                   // per slot
-    static constexpr int X_BYTES = DECODE ? EMB_PAD + KT2 * RING_BYTES : 2 * G_BYTES;
+    static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 160 KB / 128 KB
+    static constexpr int EMB_PAD = 33 * 1024;                             // decode: embedding table
+    static constexpr int X_BYTES = DECODE ? EMB_PAD : 2 * G_BYTES;
     static constexpr int OFF_BIAS = OFF_X + X_BYTES;
     static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
@@ -82,11 +88,12 @@ struct F2Cfg {
     static constexpr int OFF_CNT = OFF_BAR + NBAR * 8;
     static constexpr int OFF_TMEM = OFF_CNT + 8 * 4;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;
+    static_assert(SMEM <= 232448, "shared memory per CTA");
 };
 
 // Trace record of one role event for a unit (first CTA pair only):
 // word 0 = %globaltimer, word 1 = role | event << 4 | L << 8 | nh << 12 | tt << 16 | step << 32.
-// roles: 0 producer, 1 MMA, 2 epilogue (warp 2), 3 layer-0 builders (first warp)
+// roles: 0 producer, 1 MMA, 2 epilogue (warp 2), 3 compress layer-0 builders
 __device__ __forceinline__ void trace_ev(const Fused2Params &p, int role, int ev, int L, int nh, int tt, int step)
 {
     if (p.trace == nullptr || blockIdx.x >= 2) return;
@@ -246,7 +253,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&full[s], DECODE ? 1 + 2 : 1);   // leader producer (+ the stage's builder warp in each CTA)
+            mbar_init(&full[s], 1);                    // leader producer (+ transaction bytes)
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
@@ -281,21 +288,35 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
         if (lane == 0) {
             // ---- TMA producer (both CTAs): own activation rows + own half of the weights
             uint32_t it = 0;
+            // the embedding ring (hundreds of MB) streams from DRAM: keep it from evicting
+            // the weights and activations that live in L2
+            const uint64_t ring_policy = l2_policy_evict_first();
             for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
                 const int nkb = p.in_dim[L] / KB;
                 trace_ev(p, 0, 0, L, nh, tt, step);
-                if (L >= 1 && nh == 0) {
+                if (nh == 0 && (L >= 1 || (DECODE && step > 0))) {
+                    // layer L-1 of this tile is written (decode layer 0: the previous step's
+                    // last layer appended its token to the embedding ring)
                     const uint32_t k = (uint32_t)((DECODE ? step : grp) * NL + L - 1);
                     if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return false;
                 }
                 trace_ev(p, 0, 1, L, nh, tt, step);
+                const int ring0 = (blockIdx.x * KT2 + tt) * WIN * TM;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return false;
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(&full[s], 0);
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (L == 0 ? 0 : A_BYTES)));
-                    if (L != 0) tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
+                    const bool a_tma = DECODE || L != 0;
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (a_tma ? A_BYTES : 0)));
+                    if (L != 0) {
+                        tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
+                    } else if (DECODE) {
+                        // window position kb holds token step - 64 + kb (start-of-sequence before 0)
+                        const int tau = step - WIN + kb;
+                        const int row = tau < 0 ? (int)p.ering_sos_row : ring0 + (tau & (WIN - 1)) * TM;
+                        tma_load_2d_pair_hint(st, &p.ering, fb, 0, row, ring_policy);
+                    }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
                 trace_ev(p, 0, 2, L, nh, tt, step);
@@ -479,9 +500,14 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
                         }
                         p.state[drow] = s;
                         p.tokens_out[p.out_off[dc] + step] = (uint8_t)sym;
-                        uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
-                        ring[r * C::RING_STRIDE + (step & (WIN - 1))] = (uint8_t)sym;
+                        // append the token's embedding row to this row's window ring
+                        const int4 *e = reinterpret_cast<const int4 *>(xbuf + sym * EMB_DIM);
+                        int4 *dst = reinterpret_cast<int4 *>(
+                            p.ering_ptr + (((size_t)(blockIdx.x * KT2 + tt) * WIN + (step & (WIN - 1))) * TM + r) * KB);
+#pragma unroll
+                        for (int i = 0; i < KB / 16; ++i) dst[i] = e[i];
                     }
+                    fence_proxy_async_global();          // the ring block is read by TMA next step
                 }
             }
             tc_fence_before();
@@ -493,65 +519,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
             return true;
         });
-    } else if (DECODE) {
-        // ---- warps 10-13: layer-0 activation stages of this CTA's 128 rows from the
-        // embedding table and the window rings.  Builder warp b owns ring stage b: it
-        // takes part in every iteration of that stage (its arrival is part of the
-        // stage's count) and builds the activation for the layer-0 ones; the four
-        // warps overlap the cluster-scope release of one stage with building others.
-        static_assert(F2Cfg<DECODE>::STAGES == BUILD_WARPS, "one builder warp per ring stage");
-        const int bw = warp - 10;
-        const int j = lane & 7, sub = lane >> 3;
-        const uint8_t *emb_s = xbuf;
-        uint32_t it = 0;
-        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
-            const int nkb = p.in_dim[L] / KB;
-            const bool tr = bw == 0 && lane == 0 && L == 0;
-            if (tr) trace_ev(p, 3, 0, L, nh, tt, step);
-            if (L == 0 && nh == 0 && step > 0) {
-                // the window ring holds step-1's token once the slot finished its last layer
-                const uint32_t k = (uint32_t)(step * NL - 1);
-                if (!__all_sync(0xffffffffu, counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1)))) return false;
-            }
-            if (tr) trace_ev(p, 3, 1, L, nh, tt, step);
-            const uint8_t *ring = xbuf + C::EMB_PAD + tt * C::RING_BYTES;
-            for (int kb = 0; kb < nkb; ++kb, ++it) {
-                const int s = it % C::STAGES;
-                if (s != bw) continue;
-                if (!__all_sync(0xffffffffu, mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)))
-                    return false;
-                if (L == 0) {
-                    uint8_t *a_st = smem + s * C::STAGE_BYTES;
-                    const int pos = step - WIN + kb;
-                    // rows sub, sub+4, ...: per batch all token reads, then all embedding
-                    // reads, then all stores, so the shared-memory latencies overlap
-#pragma unroll 1
-                    for (int b0 = 0; b0 < TM / 4; b0 += 8) {
-                        int tok[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int rrow = sub + 4 * (b0 + i);
-                            tok[i] = pos < 0 ? SC_SOS : ring[rrow * C::RING_STRIDE + (pos & (WIN - 1))];
-                        }
-                        int4 v[8];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            v[i] = *reinterpret_cast<const int4 *>(emb_s + tok[i] * EMB_DIM + j * 16);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int rrow = sub + 4 * (b0 + i);
-                            *reinterpret_cast<int4 *>(a_st + sw128_offset(rrow, j)) = v[i];
-                        }
-                    }
-                    fence_proxy_async_smem();
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(map_to_rank(&full[s], 0));
-            }
-            if (tr) trace_ev(p, 3, 2, L, nh, tt, step);
-            return true;
-        });
-    } else if (warp < 12) {
+    } else if (!DECODE && warp < 12) {
         // ---- warps 10-11 (compress): sliding embedding buffer of this CTA's tile
         const int tw = threadIdx.x - 320;        // 0..63
         const int j = tw & 7, r0 = tw >> 3;

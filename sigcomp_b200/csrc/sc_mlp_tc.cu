@@ -555,6 +555,13 @@ void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_
     count_launch();
 }
 
+// The start-of-sequence block of the decoder's embedding ring: 128 copies of E[SOS].
+__global__ void k_sos_block(int8_t *dst, const int8_t *emb)
+{
+    reinterpret_cast<int4 *>(dst)[threadIdx.x] =
+        reinterpret_cast<const int4 *>(emb + (size_t)SC_SOS * EMB_DIM)[threadIdx.x & (EMB_DIM / 16 - 1)];
+}
+
 void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32_t *tile_maxlen,
                   const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
                   const int64_t *out_off, uint8_t *errors, int64_t work_rows, cudaStream_t s)
@@ -568,6 +575,15 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
         if (n_pt > (int64_t)(grid / 2) * KT2) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
         Fused2Params p{};
         fused2_common(m, p, grid, s);
+        // embedding ring: [grid][KT2][WIN] blocks of 128 rows x 128 B, then the SOS block
+        const int64_t ring_rows = (int64_t)grid * KT2 * WIN * TM;
+        int8_t *ring = (int8_t *)m->ws_ering.get((size_t)(ring_rows + TM) * KB, s);
+        k_sos_block<<<1, TM * KB / 16, 0, s>>>(ring + ring_rows * KB, m->emb);
+        SC_LAUNCH_CHECK();
+        count_launch();
+        p.ering = make_tmap(ring, KB, ring_rows + TM, KB, TM);
+        p.ering_ptr = ring;
+        p.ering_sos_row = ring_rows;
         p.n_tiles = (int)n_tiles;
         p.order = order;
         p.n_rows = n_rows;

@@ -180,6 +180,23 @@ __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *tma
         : "memory");
 }
 
+// Same with an L2 cache policy (from l2_policy_evict_first and the like).
+__device__ __forceinline__ void tma_load_2d_pair_hint(void *smem_dst, const void *tmap, uint32_t bar_cluster,
+                                                      int32_t x, int32_t y, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(smem_u32(smem_dst)), "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
+// L2 policy for data streamed once from DRAM: evict it first.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
