@@ -69,8 +69,9 @@ struct Fused2Params {
 namespace {
 
 constexpr int B_HALF = (TN / 2) * KB;          // 16 KB: this CTA's half of a weight K block
-constexpr int EPI_WARPS = 8;                    // epilogue warps per CTA (two per TMEM lane quarter)
-constexpr int BUILD_WARPS = 4;                  // compress: warps 10-11 fill the sliding buffers
+constexpr int EPI_PER_Q = 3;                    // epilogue warps per TMEM lane quarter
+constexpr int EPI_WARPS = 4 * EPI_PER_Q;        // epilogue warps per CTA
+constexpr int BUILD_WARPS = 2;                  // compress: the last two warps fill the sliding buffers
 constexpr int FUSED2_THREADS = 32 * (2 + EPI_WARPS + BUILD_WARPS);
 constexpr int BIAS_MAX = FMAX_LAYERS * MAX_N;   // int32 entries
 
@@ -231,7 +232,7 @@ __device__ __forceinline__ void mma_k_block_pair(uint32_t d, uint32_t a_addr, ui
 }
 
 template <bool DECODE>
-__global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused2Params p)
+__global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_constant__ Fused2Params p)
 {
     using C = F2Cfg<DECODE>;
     extern __shared__ uint8_t smem_raw[];
@@ -358,13 +359,13 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             });
         }
     } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
-        // ---- epilogue warps: TMEM lane quarter q; hidden layers split the 256 columns of
-        // a unit between the two warps of a quarter.  The last layer of a unit runs on
-        // one warp of the quarter, the two warps taking turns: by tile slot for decoding
-        // (so a row's coder state always stays with the warp that wrote it), by unit for
-        // compression.
+        // ---- epilogue warps: TMEM lane quarter q; hidden layers split the eight
+        // 32-column chunks of a unit between the EPI_PER_Q warps of a quarter.  The last
+        // layer of a unit runs on one warp of the quarter, the warps taking turns: by tile
+        // slot for decoding (so a row's coder state always stays with the warp that wrote
+        // it), by unit for compression.
         const int q = warp & 3;
-        const int half = (warp - 2) >> 2;
+        const int part = (warp - 2) >> 2;
         const int r = q * 32 + lane;
         uint32_t uu = 0, lu = 0;
         for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
@@ -373,7 +374,7 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             if (tr) trace_ev(p, 2, 0, L, nh, tt, step);
             bool mine = false;
             if (L == NL - 1) {
-                mine = DECODE ? (((tt + grp) & 1) == half) : ((int)(lu & 1) == half);
+                mine = DECODE ? ((tt + grp) % EPI_PER_Q == part) : ((int)(lu % EPI_PER_Q) == part);
                 ++lu;
             }
             // decoding: this row's coder state and quotient, fetched before the logits are ready
@@ -412,29 +413,22 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             if (L < NL - 1) {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
 #pragma unroll 1
-                for (int c = half * 4; c < half * 4 + 4; c += 2) {
-                    uint32_t va[32], vb[32];
+                for (int c = part; c < TN / 32; c += EPI_PER_Q) {
+                    uint32_t va[32];
                     tmem_ld32(taddr + c * 32, va);
-                    tmem_ld32(taddr + c * 32 + 32, vb);
                     tmem_ld_wait();
                     const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
-                    uint32_t packed[16];
+                    uint32_t packed[8];
                     if (rq_fast) {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            packed[8 + i] = requant4_hi(&vb[4 * i], bv[8 + i], rq_m0, rq_hs, rq_relu, rq_one);
                     } else {
 #pragma unroll
                         for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) packed[8 + i] = requant4(&vb[4 * i], bv[8 + i], rq);
                     }
                     uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i)
-                        dst[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+                    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+                    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -519,9 +513,9 @@ __global__ void __launch_bounds__(448, 1) k_fused2(const __grid_constant__ Fused
             if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
             return true;
         });
-    } else if (!DECODE && warp < 12) {
-        // ---- warps 10-11 (compress): sliding embedding buffer of this CTA's tile
-        const int tw = threadIdx.x - 320;        // 0..63
+    } else if (!DECODE) {
+        // ---- last two warps (compress): sliding embedding buffer of this CTA's tile
+        const int tw = threadIdx.x - 32 * (2 + EPI_WARPS);   // 0..63
         const int j = tw & 7, r0 = tw >> 3;
         uint32_t li = 0;
         for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
