@@ -303,14 +303,19 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 trace_ev(p, 0, 1, L, nh, tt, step);
                 const int ring0 = (blockIdx.x * KT2 + tt) * WIN * TM;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                // compress layer 0 reads A from the sliding buffer: its stages carry the
+                // weights of two K blocks (the second in the unused activation half)
+                const int kstep = (!DECODE && L == 0) ? 2 : 1;
+                for (int kb = 0; kb < nkb; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return false;
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(&full[s], 0);
                     const bool a_tma = DECODE || L != 0;
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (a_tma ? A_BYTES : 0)));
-                    if (L != 0) {
+                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (a_tma ? A_BYTES : B_HALF)));
+                    if (kstep == 2) {
+                        tma_load_2d_pair(st, &p.w[L], fb, (kb + 1) * KB, nh * TN + (int)rank * (TN / 2));
+                    } else if (L != 0) {
                         tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
                     } else if (DECODE) {
                         // window position kb holds token step - 64 + kb (start-of-sequence before 0)
@@ -338,14 +343,20 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
                 tc_fence_after();
                 const uint32_t d = tmem_base + ab * TN;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int kstep = (!DECODE && L == 0) ? 2 : 1;
+                for (int kb = 0; kb < nkb; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
                     if (L == 0 && kb < 4) trace_ev(p, 1, 3, L, kb, tt, step);
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
-                    const uint32_t a_addr = (!DECODE && L == 0) ? smem_u32(xbuf + gb * G_BYTES) + kb * KB : st;
-                    mma_k_block_pair(d, a_addr, st + A_BYTES, kb == 0);
+                    if (kstep == 2) {
+                        const uint32_t g = smem_u32(xbuf + gb * G_BYTES);
+                        mma_k_block_pair(d, g + kb * KB, st + A_BYTES, kb == 0);
+                        mma_k_block_pair(d, g + (kb + 1) * KB, st, false);
+                    } else {
+                        mma_k_block_pair(d, st, st + A_BYTES, kb == 0);
+                    }
                     mma_commit_pair(&empty[s], 0x3);
                 }
                 mma_commit_pair(&acc_full[ab], 0x3);
