@@ -77,11 +77,13 @@ constexpr int BIAS_MAX = FMAX_LAYERS * MAX_N;   // int32 entries
 
 template <bool DECODE>
 struct F2Cfg {
-    static constexpr int STAGES = DECODE ? 5 : 4;
-    static constexpr int STAGE_BYTES = A_BYTES + B_HALF;                  // 32 KB
-    static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 160 KB / 128 KB
-    static constexpr int EMB_PAD = 33 * 1024;                             // decode: embedding table
-    static constexpr int X_BYTES = DECODE ? EMB_PAD : 2 * G_BYTES;
+    // decode: layer 0 is one pass over K for both 256-column halves (two accumulators),
+    // so a stage holds the ring block and both weight halves: the block is read from
+    // the ring once per step instead of twice
+    static constexpr int STAGES = 4;
+    static constexpr int STAGE_BYTES = A_BYTES + (DECODE ? 2 : 1) * B_HALF;   // 48 KB / 32 KB
+    static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 192 KB / 128 KB
+    static constexpr int X_BYTES = DECODE ? 0 : 2 * G_BYTES;
     static constexpr int OFF_BIAS = OFF_X + X_BYTES;
     static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
@@ -273,11 +275,6 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
     for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = p.lut[i];
     for (int l = 0; l < NL; ++l)
         for (int i = threadIdx.x; i < p.out_dim[l]; i += blockDim.x) bias_s[l * MAX_N + i] = p.bias[l][i];
-    if (DECODE) {
-        const int4 *srcv = reinterpret_cast<const int4 *>(p.emb);
-        int4 *dst = reinterpret_cast<int4 *>(xbuf);
-        for (int i = threadIdx.x; i < EMB_BYTES / 16; i += blockDim.x) dst[i] = srcv[i];
-    }
     tc_fence_before();
     __syncthreads();
     cluster_sync();                       // both CTAs' barriers exist before any remote use
@@ -293,6 +290,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             // the weights and activations that live in L2
             const uint64_t ring_policy = l2_policy_evict_first();
             for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+                if (DECODE && L == 0 && nh == 1) return true;       // loaded with half 0
                 const int nkb = p.in_dim[L] / KB;
                 trace_ev(p, 0, 0, L, nh, tt, step);
                 if (nh == 0 && (L >= 1 || (DECODE && step > 0))) {
@@ -312,7 +310,9 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(&full[s], 0);
                     const bool a_tma = DECODE || L != 0;
-                    if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (B_HALF + (a_tma ? A_BYTES : B_HALF)));
+                    const bool dual = DECODE && L == 0;
+                    if (rank == 0)
+                        mbar_arrive_expect_tx(&full[s], 2 * ((dual ? 2 : 1) * B_HALF + (a_tma ? A_BYTES : B_HALF)));
                     if (kstep == 2) {
                         tma_load_2d_pair(st, &p.w[L], fb, (kb + 1) * KB, nh * TN + (int)rank * (TN / 2));
                     } else if (L != 0) {
@@ -322,6 +322,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                         const int tau = step - WIN + kb;
                         const int row = tau < 0 ? (int)p.ering_sos_row : ring0 + (tau & (WIN - 1)) * TM;
                         tma_load_2d_pair_hint(st, &p.ering, fb, 0, row, ring_policy);
+                        tma_load_2d_pair(st + A_BYTES + B_HALF, &p.w[L], fb, kb * KB, TN + (int)rank * (TN / 2));
                     }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
@@ -334,10 +335,14 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             // ---- MMA issuer (leader CTA only)
             uint32_t it = 0, uu = 0, li = 0;
             for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+                // decoding layer 0: half 1 accumulates in the other buffer during half 0's pass
+                if (DECODE && L == 0 && nh == 1) return true;
+                const bool dual = DECODE && L == 0;
                 const int nkb = p.in_dim[L] / KB;
                 const int ab = uu & 1;
                 trace_ev(p, 1, 0, L, nh, tt, step);
                 if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
+                if (dual && !mbar_wait_cluster(&acc_empty[ab ^ 1], (((uu + 1) >> 1) & 1) ^ 1)) return false;
                 trace_ev(p, 1, 1, L, nh, tt, step);
                 const int gb = li & 1;
                 if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
@@ -356,12 +361,14 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                         mma_k_block_pair(d, g + (kb + 1) * KB, st, false);
                     } else {
                         mma_k_block_pair(d, st, st + A_BYTES, kb == 0);
+                        if (dual) mma_k_block_pair(tmem_base + (ab ^ 1) * TN, st, st + A_BYTES + B_HALF, kb == 0);
                     }
                     mma_commit_pair(&empty[s], 0x3);
                 }
                 mma_commit_pair(&acc_full[ab], 0x3);
+                if (dual) mma_commit_pair(&acc_full[ab ^ 1], 0x3);
                 trace_ev(p, 1, 2, L, nh, tt, step);
-                ++uu;
+                uu += dual ? 2 : 1;
                 if (!DECODE && L == 0 && nh == p.out_dim[0] / TN - 1) {
                     mma_commit_pair(&g_empty[gb], 0x3);
                     ++li;
@@ -506,7 +513,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                         p.state[drow] = s;
                         p.tokens_out[p.out_off[dc] + step] = (uint8_t)sym;
                         // append the token's embedding row to this row's window ring
-                        const int4 *e = reinterpret_cast<const int4 *>(xbuf + sym * EMB_DIM);
+                        const int4 *e = reinterpret_cast<const int4 *>(p.emb + sym * EMB_DIM);
                         int4 *dst = reinterpret_cast<int4 *>(
                             p.ering_ptr + (((size_t)(blockIdx.x * KT2 + tt) * WIN + (step & (WIN - 1))) * TM + r) * KB);
 #pragma unroll
