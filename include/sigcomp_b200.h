@@ -135,6 +135,41 @@ SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t
                          void *stream);
 
 /*
+ * SigComp's signal split on the device: _split_signal (sigcomp/main.py:504-521)
+ * of every read, after the lossy step _lossy_encode(_reduce_lsb(read, lsb), lsb)
+ * (main.py:158-171) when lsb > 0.  Every array is in device memory.
+ *   samples        int16 [sample_offsets[n_reads]]   reads, concatenated (each >= 1 sample)
+ *   sample_offsets int64 [n_reads + 1]
+ *   lsb            0 (lossless) .. 15
+ * Outputs (capacity of tokens/large/large_pos: sample_offsets[n_reads] - n_reads):
+ *   sig0           int16  [n_reads]        first sample of each read (after the lossy step)
+ *   tokens         uint8  []               zig-zag deltas below 256, read after read: the
+ *                                          codec's input (main.py:862-873)
+ *   token_offsets  int64  [n_reads + 1]
+ *   large          uint16 []               the other deltas, minus 256
+ *   large_pos      uint32 []               their position deltas (first position, then gaps - 1)
+ *   large_offsets  int64  [n_reads + 1]
+ * An empty read returns SC_ERR_INVALID_ARGUMENT (the reference fails on sig[0]).
+ */
+SC_API int sc_split_signal_device(sc_model *model, const int16_t *samples, const int64_t *sample_offsets,
+                                  int64_t n_reads, int32_t lsb, int16_t *sig0, uint8_t *tokens,
+                                  int64_t *token_offsets, uint16_t *large, uint32_t *large_pos,
+                                  int64_t *large_offsets, void *stream);
+
+/*
+ * Inverse on the device: _reassemble_signal (sigcomp/main.py:524-546) with the
+ * large values and position deltas given decoded, then _lossy_decode
+ * (main.py:170-171) when lsb > 0.  Same array layout as sc_split_signal_device;
+ * samples (output) has sample_offsets[n_reads] entries.  Streams that do not
+ * describe reads of the given lengths return SC_ERR_INVALID_ARGUMENT.
+ */
+SC_API int sc_reassemble_signal_device(sc_model *model, const int16_t *sig0, const int64_t *sample_offsets,
+                                       int64_t n_reads, int32_t lsb, const uint8_t *tokens,
+                                       const int64_t *token_offsets, const uint16_t *large,
+                                       const uint32_t *large_pos, const int64_t *large_offsets,
+                                       int16_t *samples, void *stream);
+
+/*
  * sc_mlp_logits_device without any device allocation.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc, such as a host
  * framework that has reserved the GPU's memory for its own pool, or a

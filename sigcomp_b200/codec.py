@@ -139,6 +139,84 @@ class B200Compression:
         _lib.check(rc, "sc_decompress_chunks")
         return out[:int(lengths.sum())]
 
+    # -- signal transform on the device (main.py:504-546) ----------------------
+    def split_signals(self, reads, lsb=0):
+        """``_split_signal`` of every int16 read on the GPU (after the lossy step when lsb > 0).
+
+        Returns one ``(sig0, tokens uint8, large uint16 minus 256, position deltas uint32)``
+        per read, like ``sigcomp.main._split_signal``.
+        """
+        import torch
+        reads = [np.ascontiguousarray(r, dtype=np.int16) for r in reads]
+        if any(len(r) == 0 for r in reads):
+            raise ValueError("Every read must hold at least one sample")
+        n = len(reads)
+        if n == 0:
+            return []
+        off = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum([len(r) for r in reads], out=off[1:])
+        dev = torch.device(self.device)
+        x = torch.from_numpy(np.concatenate(reads)).to(dev)
+        d_off = torch.from_numpy(off).to(dev)
+        cap = max(int(off[-1]) - n, 1)
+        sig0 = torch.empty(n, dtype=torch.int16, device=dev)
+        tok = torch.empty(cap, dtype=torch.uint8, device=dev)
+        tok_off = torch.empty(n + 1, dtype=torch.int64, device=dev)
+        large = torch.empty(cap, dtype=torch.int16, device=dev)
+        pos = torch.empty(cap, dtype=torch.int32, device=dev)
+        large_off = torch.empty(n + 1, dtype=torch.int64, device=dev)
+        vp = ctypes.c_void_p
+        rc = self._lib.sc_split_signal_device(
+            self._handle, vp(x.data_ptr()), vp(d_off.data_ptr()), n, int(lsb), vp(sig0.data_ptr()),
+            vp(tok.data_ptr()), vp(tok_off.data_ptr()), vp(large.data_ptr()), vp(pos.data_ptr()),
+            vp(large_off.data_ptr()), vp(torch.cuda.current_stream(dev).cuda_stream))
+        _lib.check(rc, "sc_split_signal_device")
+        s0, to, lo = sig0.cpu().numpy(), tok_off.cpu().numpy(), large_off.cpu().numpy()
+        t, lv, lp = tok.cpu().numpy(), large.cpu().numpy().view(np.uint16), pos.cpu().numpy().view(np.uint32)
+        return [(int(s0[i]), t[to[i]:to[i + 1]].copy(), lv[lo[i]:lo[i + 1]].copy(), lp[lo[i]:lo[i + 1]].copy())
+                for i in range(n)]
+
+    def reassemble_signals(self, splits, lengths, lsb=0):
+        """Inverse of :meth:`split_signals`: ``_reassemble_signal`` (then ``_lossy_decode``) on the GPU."""
+        import torch
+        n = len(splits)
+        if n != len(lengths):
+            raise ValueError("splits and lengths differ in length")
+        if n == 0:
+            return []
+        lengths = np.asarray(lengths, dtype=np.int64)
+        if np.any(lengths < 1):
+            raise ValueError("Every read must hold at least one sample")
+        off = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum(lengths, out=off[1:])
+        to = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum([len(sp[1]) for sp in splits], out=to[1:])
+        lo = np.zeros(n + 1, dtype=np.int64)
+        np.cumsum([len(sp[2]) for sp in splits], out=lo[1:])
+        if any(len(sp[2]) != len(sp[3]) for sp in splits):
+            raise ValueError("large values and position deltas differ in length")
+        dev = torch.device(self.device)
+
+        def cat(parts, dtype, view):
+            a = np.concatenate([np.asarray(p_, dtype=dtype) for p_ in parts]) if parts else np.zeros(0, dtype)
+            a = a if len(a) else np.zeros(1, dtype)
+            return torch.from_numpy(a.view(view)).to(dev)
+
+        sig0 = torch.from_numpy(np.asarray([sp[0] for sp in splits], dtype=np.int16)).to(dev)
+        tok = cat([sp[1] for sp in splits], np.uint8, np.uint8)
+        large = cat([sp[2] for sp in splits], np.uint16, np.int16)
+        pos = cat([sp[3] for sp in splits], np.uint32, np.int32)
+        d_off, d_to, d_lo = (torch.from_numpy(a).to(dev) for a in (off, to, lo))
+        out = torch.empty(int(off[-1]), dtype=torch.int16, device=dev)
+        vp = ctypes.c_void_p
+        rc = self._lib.sc_reassemble_signal_device(
+            self._handle, vp(sig0.data_ptr()), vp(d_off.data_ptr()), n, int(lsb), vp(tok.data_ptr()),
+            vp(d_to.data_ptr()), vp(large.data_ptr()), vp(pos.data_ptr()), vp(d_lo.data_ptr()),
+            vp(out.data_ptr()), vp(torch.cuda.current_stream(dev).cuda_stream))
+        _lib.check(rc, "sc_reassemble_signal_device")
+        o = out.cpu().numpy()
+        return [o[off[i]:off[i + 1]].copy() for i in range(n)]
+
     # -- chunk level (QuantMLPCompression interface) ---------------------------
     def compress_chunks(self, chunks, max_batch_size=64, use_perfect=False, use_tqdm=False):
         if max_batch_size < 1:

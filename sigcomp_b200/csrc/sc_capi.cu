@@ -30,6 +30,13 @@ int compress_device(sc_model *m, const uint8_t *tokens, const int64_t *off_d, co
 int decompress_device(sc_model *m, const uint32_t *words, const int64_t *word_offsets, const int64_t *lengths_d,
                       const int64_t *lengths_h, int64_t n, uint8_t *tokens, uint8_t *errors_d, cudaStream_t s);
 void run_mlp(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
+int split_signal_device(sc_model *m, const int16_t *samples, const int64_t *off_d, const int64_t *off_h,
+                        int64_t n_reads, int lsb, int16_t *sig0, uint8_t *small, int64_t *small_off,
+                        uint16_t *large, uint32_t *large_pos, int64_t *large_off, cudaStream_t s);
+int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *off_d, int64_t n_reads, int lsb,
+                             const uint8_t *small, const int64_t *small_off, const uint16_t *large,
+                             const uint32_t *large_pos, const int64_t *large_off, int16_t *samples,
+                             cudaStream_t s);
 
 namespace {
 
@@ -470,6 +477,74 @@ int64_t sc_trace_read(sc_model *m, int32_t cta, uint64_t *records, int64_t capac
         return SC_OK;
     });
     return rc == SC_OK ? n : -1;
+}
+
+// read offsets of a signal call: nondecreasing, every read at least one sample
+static int check_read_offsets(const int64_t *off, int64_t n)
+{
+    if (off[0] != 0) {
+        set_error("sample_offsets[0] must be 0");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    for (int64_t r = 0; r < n; ++r)
+        if (off[r + 1] - off[r] < 1) {
+            set_error("read %lld has no samples", (long long)r);
+            return SC_ERR_INVALID_ARGUMENT;
+        }
+    return SC_OK;
+}
+
+int sc_split_signal_device(sc_model *m, const int16_t *samples, const int64_t *sample_offsets, int64_t n_reads,
+                           int32_t lsb, int16_t *sig0, uint8_t *tokens, int64_t *token_offsets, uint16_t *large,
+                           uint32_t *large_pos, int64_t *large_offsets, void *stream)
+{
+    g_err[0] = 0;
+    if (!m || n_reads < 0 || lsb < 0 || lsb > 15 || !sample_offsets || !token_offsets || !large_offsets ||
+        (n_reads > 0 && (!samples || !sig0 || !tokens || !large || !large_pos))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        std::vector<int64_t> off_h(n_reads + 1);
+        SC_CUDA(cudaMemcpyAsync(off_h.data(), sample_offsets, sizeof(int64_t) * (n_reads + 1),
+                                cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        int rc = check_read_offsets(off_h.data(), n_reads);
+        if (rc) return rc;
+        split_signal_device(m, samples, sample_offsets, off_h.data(), n_reads, lsb, sig0, tokens, token_offsets,
+                            large, large_pos, large_offsets, s);
+        SC_CUDA(cudaStreamSynchronize(s));
+        return SC_OK;
+    });
+}
+
+int sc_reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *sample_offsets, int64_t n_reads,
+                                int32_t lsb, const uint8_t *tokens, const int64_t *token_offsets,
+                                const uint16_t *large, const uint32_t *large_pos, const int64_t *large_offsets,
+                                int16_t *samples, void *stream)
+{
+    g_err[0] = 0;
+    if (!m || n_reads < 0 || lsb < 0 || lsb > 15 || !sample_offsets || !token_offsets || !large_offsets ||
+        (n_reads > 0 && (!sig0 || !samples))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        std::vector<int64_t> off_h(n_reads + 1);
+        SC_CUDA(cudaMemcpyAsync(off_h.data(), sample_offsets, sizeof(int64_t) * (n_reads + 1),
+                                cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        int rc = check_read_offsets(off_h.data(), n_reads);
+        if (rc) return rc;
+        if (reassemble_signal_device(m, sig0, sample_offsets, n_reads, lsb, tokens, token_offsets, large, large_pos,
+                                     large_offsets, samples, s)) {
+            set_error("token and large-value streams do not match the read lengths");
+            return SC_ERR_INVALID_ARGUMENT;
+        }
+        return SC_OK;
+    });
 }
 
 int sc_mlp_logits_device(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, void *stream)
