@@ -3,24 +3,29 @@
 
 Metric: compress & decompress Msamples/s at 1/2/4/8 B200, with
 bits/sample, bit-exact.  A step is one compress + decompress round trip of a
-batch of synthetic reads drawn from the configuration-2 generator (R10.4.1-like,
-lognormal lengths, median 30,000 samples) with the bundled lossless model and
-chunk_len 2048.  Each rank holds its own batch (weak scaling, reads sharded by
-rank, no collective on the data path); after each compress the ranks exchange
-their stream byte counts (all-gather of one int64), which is how a sharded run
-lays out the archive.
+batch of synthetic int16 reads drawn from the configuration-2 generator
+(R10.4.1-like, lognormal lengths, median 30,000 samples) with the bundled
+lossless model and chunk_len 2048, the SigComp per-read path on the device:
 
-  value      whole-job round-trip Msamples/s with tokens resident in HBM
-             (device entry points sc_compress_chunks_device / sc_decompress_chunks_device)
-  e2e        the same through the host entry points (sc_compress_chunks /
-             sc_decompress_chunks) from pinned host memory, copies timed
+  compress    split every read (sc_split_signal_device: delta / zig-zag / split of
+              main.py:504-521) -> chunk the token streams -> sc_compress_chunks_device
+  decompress  sc_decompress_chunks_device -> sc_reassemble_signal_device -> int16 reads
+
+Each rank holds its own batch (weak scaling, reads sharded by rank, no collective
+on the data path); after each compress the ranks exchange their stream byte
+counts (all-gather of one int64), which is how a sharded run lays out the archive.
+
+  value      whole-job round-trip Msamples/s with the reads resident in HBM
+  e2e        the same with every step's reads copied in from pinned host memory,
+             the compressed record streams (words, large values, positions, offsets)
+             copied out and back in, and the decoded reads copied out
   roofline   the dominant kernel (the persistent autoregressive decoder, all nine
              tcgen05 int8 layers + frequency search + range decoding in one launch)
              against the int8 tensor throughput measured in the same run with
              torch._int_mm; roofline_compress does the same for the fused compress
              kernel
-  cpu_baseline  the CPU port of the reference codec (int_mm + C coder, oracle/)
-             on a bounded sample, rank 0 at N=1
+  cpu_baseline  the CPU port of the reference codec (numpy split + int_mm GEMMs + C
+             coder, oracle/) on a bounded sample, rank 0 at N=1
 
 `--impl reference` times that CPU port alone on the host cores.
 """
@@ -30,7 +35,6 @@ import json
 import os
 import subprocess
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -44,6 +48,8 @@ UNIT = "Msamples/s"
 CHUNK_LEN = 2048
 # int8 MLP work per coded token: 2 x (8192*512 + 7*512*512 + 512*256) multiply-adds
 OPS_PER_TOKEN = 2 * (8192 * 512 + 7 * 512 * 512 + 512 * 256)
+WORKLOAD = ("r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, levels N(500,60), "
+            "dwell 12, noise 12), lossless model")
 
 
 def parse_args():
@@ -63,19 +69,24 @@ def parse_args():
     return ap.parse_args()
 
 
-def make_batch(rank, n_reads, chunk_len=CHUNK_LEN):
-    """Token chunks of one rank's batch: (samples, tokens, offsets, per-read token counts)."""
-    from sigcomp_b200 import signal, synthetic
+def make_reads(rank, n_reads):
+    """One rank's batch of int16 reads: (reads, concatenated samples, sample offsets)."""
+    from sigcomp_b200 import synthetic
     reads = synthetic.make_reads("r10_lognormal", seed=1000 + rank, count=n_reads)
-    samples = int(sum(len(r) for r in reads))
-    toks = [signal.split_signal(r)[1] for r in reads]
-    lengths = []
-    for t in toks:
-        lengths += [min(chunk_len, len(t) - i) for i in range(0, len(t), chunk_len)]
-    offsets = np.zeros(len(lengths) + 1, dtype=np.int64)
-    np.cumsum(lengths, out=offsets[1:])
-    tokens = np.concatenate(toks).astype(np.uint8)
-    return samples, tokens, offsets, np.asarray([len(t) for t in toks])
+    off = np.zeros(len(reads) + 1, dtype=np.int64)
+    np.cumsum([len(r) for r in reads], out=off[1:])
+    return reads, np.concatenate(reads), off
+
+
+def chunk_offsets(tok_off, chunk_len):
+    """Chunk boundaries of per-read token streams (SigComp cuts each read's tokens
+    into chunk_len pieces, cpu_compression.py:28-50): int64 offsets into the tokens."""
+    ntok = np.diff(tok_off)
+    nch = (ntok + chunk_len - 1) // chunk_len
+    first = np.repeat(tok_off[:-1], nch)
+    within = np.arange(int(nch.sum()), dtype=np.int64) - np.repeat(np.cumsum(nch) - nch, nch)
+    starts = first + within * chunk_len
+    return np.append(starts, tok_off[-1]).astype(np.int64)
 
 
 class ClockSampler:
@@ -146,30 +157,39 @@ def int8_peak_tops():
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
-def cpu_round_trip(tokens, offsets, samples, steps=1, warmup=1):
-    """The reference codec ported to the CPU (oracle/, int_mm GEMMs + C coder)."""
+def cpu_round_trip(reads, chunk_len, steps=1, warmup=1):
+    """The reference path ported to the CPU: numpy split / reassembly (sigcomp_b200.signal,
+    pinned to the reference's outputs) around the oracle codec (int_mm GEMMs + C coder)."""
     import torch
     from oracle.oracle import OracleModel
+    from sigcomp_b200 import signal
     from sigcomp_b200.model import load_model
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     om = OracleModel(load_model(name="lossless"))
-    chunks = [tokens[offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]
-    lengths = [len(c) for c in chunks]
+    samples = int(sum(len(r) for r in reads))
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        streams = om.compress_chunks(chunks, chunk_len=CHUNK_LEN, backend="int_mm")
+        splits = [signal.split_signal(r) for r in reads]
+        chunks = [sp[1][j:j + chunk_len] for sp in splits for j in range(0, len(sp[1]), chunk_len)]
+        streams = om.compress_chunks(chunks, chunk_len=chunk_len, backend="int_mm")
         t1 = time.perf_counter()
-        back = om.decompress_chunks(streams, lengths, chunk_len=CHUNK_LEN, backend="int_mm")
+        back = om.decompress_chunks(streams, [len(c) for c in chunks], chunk_len=chunk_len, backend="int_mm")
+        pos, out = 0, []
+        for r, sp in zip(reads, splits):
+            k = (len(sp[1]) + chunk_len - 1) // chunk_len
+            tok = np.concatenate(back[pos:pos + k]) if k else np.zeros(0, np.uint8)
+            pos += k
+            out.append(signal.reassemble_signal(sp[0], len(r), tok, sp[2], sp[3]))
         t2 = time.perf_counter()
         if i >= warmup:
             times.append((t1 - t0, t2 - t1))
-        assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+        assert all(np.array_equal(a, b) for a, b in zip(out, reads))
     tc = sum(t[0] for t in times) / len(times)
     td = sum(t[1] for t in times) / len(times)
     return {"value": samples / (tc + td) / 1e6, "compress": samples / tc / 1e6, "decompress": samples / td / 1e6,
-            "cores": cores, "seconds_per_step": tc + td}
+            "cores": cores, "seconds_per_step": tc + td, "samples": samples}
 
 
 def run_reference(args):
@@ -177,17 +197,16 @@ def run_reference(args):
     if rank != 0:
         return 0
     n_reads = args.cpu_reads
-    samples, tokens, offsets, _ = make_batch(0, n_reads)
-    r = cpu_round_trip(tokens, offsets, samples, steps=args.steps, warmup=args.warmup)
-    sample = (f"{n_reads} reads ({samples} samples, {len(offsets) - 1} chunks) of the configuration-2 "
-              "generator per step")
+    reads, _, _ = make_reads(0, n_reads)
+    r = cpu_round_trip(reads, args.chunk_len, steps=args.steps, warmup=args.warmup)
+    sample = f"{n_reads} reads ({r['samples']} samples) of the configuration-2 generator per step"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(r["seconds_per_step"] * 1e3, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "r10_lognormal (configuration 2 generator), lossless model, chunk_len 2048",
-                   "reads_per_step": n_reads, "samples_per_step": samples},
+        "config": {"workload": f"{WORKLOAD}, chunk_len {args.chunk_len}", "reads_per_step": n_reads,
+                   "samples_per_step": r["samples"]},
         "compress_msps": round(r["compress"], 4), "decompress_msps": round(r["decompress"], 4),
         "cpu_baseline": {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
                          "sample": sample},
@@ -197,12 +216,72 @@ def run_reference(args):
     return 0
 
 
+class Pipeline:
+    """Device buffers and the C-ABI calls of one rank's round trip."""
+
+    def __init__(self, codec, n_reads, n_samples, chunk_len):
+        import ctypes
+        import torch
+        self.torch, self.vp = torch, ctypes.c_void_p
+        self.L, self.h = codec._lib, codec.handle
+        self.chunk_len = chunk_len
+        self.R, self.S = n_reads, n_samples
+        dev = torch.device("cuda", torch.cuda.current_device())
+        cap = max(n_samples - n_reads, 1)
+
+        def e(n, dt):
+            return torch.empty(n, dtype=dt, device=dev)
+
+        self.x, self.y = e(n_samples, torch.int16), e(n_samples, torch.int16)
+        self.soff = e(n_reads + 1, torch.int64)
+        self.sig0 = e(n_reads, torch.int16)
+        self.tok, self.tok2 = e(cap, torch.uint8), e(cap, torch.uint8)
+        self.tok_off, self.large_off = e(n_reads + 1, torch.int64), e(n_reads + 1, torch.int64)
+        self.large, self.pos = e(cap, torch.int16), e(cap, torch.int32)
+        max_chunks = cap // chunk_len + n_reads + 1          # every read adds at most one partial chunk
+        self.word_cap = cap + 2 * max_chunks + 1
+        self.words = e(self.word_cap, torch.int32)
+        self.choff = e(max_chunks + 1, torch.int64)
+        self.chlen = e(max_chunks, torch.int64)
+        self.woff = e(max_chunks + 1, torch.int64)
+        self.stream = torch.cuda.current_stream()
+        self.n_chunks = 0
+        self.chlen_h = np.zeros(0, np.int64)
+
+    def p(self, t):
+        return self.vp(t.data_ptr())
+
+    def compress(self):
+        from sigcomp_b200 import _lib
+        L, h, p, sp = self.L, self.h, self.p, self.vp(self.stream.cuda_stream)
+        _lib.check(L.sc_split_signal_device(h, p(self.x), p(self.soff), self.R, 0, p(self.sig0), p(self.tok),
+                                            p(self.tok_off), p(self.large), p(self.pos), p(self.large_off), sp))
+        # chunk boundaries of the per-read token streams (host, from the R + 1 token offsets)
+        choff = chunk_offsets(self.tok_off.cpu().numpy(), self.chunk_len)
+        n = len(choff) - 1
+        self.n_chunks = n
+        self.chlen_h = np.ascontiguousarray(np.diff(choff), dtype=np.int64)
+        self.choff[:n + 1].copy_(self.torch.from_numpy(choff))
+        self.chlen[:n].copy_(self.torch.from_numpy(self.chlen_h))
+        _lib.check(L.sc_compress_chunks_device(h, p(self.tok), p(self.choff), n, p(self.words), self.word_cap,
+                                               p(self.woff), None, sp))
+
+    def decompress(self):
+        from sigcomp_b200 import _lib
+        L, h, p, sp = self.L, self.h, self.p, self.vp(self.stream.cuda_stream)
+        _lib.check(L.sc_decompress_chunks_device(h, p(self.words), p(self.woff), p(self.chlen),
+                                                 self.vp(self.chlen_h.ctypes.data), self.n_chunks, p(self.tok2),
+                                                 None, sp))
+        _lib.check(L.sc_reassemble_signal_device(h, p(self.sig0), p(self.soff), self.R, 0, p(self.tok2),
+                                                 p(self.tok_off), p(self.large), p(self.pos), p(self.large_off),
+                                                 p(self.y), sp))
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
 
-    import ctypes
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -217,36 +296,22 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    samples, tokens, offsets, read_tokens = make_batch(rank, args.reads, args.chunk_len)
-    n_chunks = len(offsets) - 1
-    n_tok = int(offsets[-1])
-    lengths = np.diff(offsets)
+    reads, samples_np, soff_np = make_reads(rank, args.reads)
+    n_reads, n_samples = len(reads), int(soff_np[-1])
     codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name="lossless"))
-    L = codec._lib
-    h = codec.handle
-    vp = ctypes.c_void_p
-    stream = torch.cuda.current_stream()
-    sp = vp(stream.cuda_stream)
-
-    # device-resident inputs and outputs
-    d_tok = torch.from_numpy(tokens).cuda()
-    d_off = torch.from_numpy(offsets).cuda()
-    d_len = torch.from_numpy(lengths.astype(np.int64)).cuda()
-    cap = n_tok + 2 * n_chunks + 1
-    d_words = torch.empty(cap, dtype=torch.int32, device="cuda")
-    d_woff = torch.empty(n_chunks + 1, dtype=torch.int64, device="cuda")
-    d_back = torch.empty(max(n_tok, 1), dtype=torch.uint8, device="cuda")
-    lengths_h = np.ascontiguousarray(lengths, dtype=np.int64)
+    pl = Pipeline(codec, n_reads, n_samples, args.chunk_len)
+    pl.x.copy_(torch.from_numpy(samples_np))
+    pl.soff.copy_(torch.from_numpy(soff_np))
     counts = torch.zeros(world, dtype=torch.int64, device="cuda")
 
-    def step():
-        _lib.check(L.sc_compress_chunks_device(h, vp(d_tok.data_ptr()), vp(d_off.data_ptr()), n_chunks,
-                                               vp(d_words.data_ptr()), cap, vp(d_woff.data_ptr()), None, sp))
+    def exchange():
         if world > 1:   # archive layout: every rank learns every shard's stream size
-            dist.all_gather_into_tensor(counts, d_woff[-1:].contiguous())
-        _lib.check(L.sc_decompress_chunks_device(h, vp(d_words.data_ptr()), vp(d_woff.data_ptr()),
-                                                 vp(d_len.data_ptr()), vp(lengths_h.ctypes.data), n_chunks,
-                                                 vp(d_back.data_ptr()), None, sp))
+            dist.all_gather_into_tensor(counts, pl.woff[pl.n_chunks:pl.n_chunks + 1].contiguous())
+
+    def step():
+        pl.compress()
+        exchange()
+        pl.decompress()
 
     def sync():
         torch.cuda.synchronize()
@@ -256,13 +321,16 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    ok = bool(torch.equal(d_back[:n_tok], d_tok))
-    n_words = int(d_woff[-1].item())
+    ok = bool(torch.equal(pl.y, pl.x))
+    n_tok = int(pl.tok_off[-1].item())
+    n_large = int(pl.large_off[-1].item())
+    n_chunks = pl.n_chunks
+    n_words = int(pl.woff[n_chunks].item())
     # bits: framed neural streams (2-byte frame per chunk + words) over the samples
     stream_bytes = 4 * n_words + 2 * n_chunks
 
     # timed region (device-resident), with per-phase events and per-kernel profiling
-    _lib.profile_enable(h, True)
+    _lib.profile_enable(codec.handle, True)
     launches0 = _lib.kernel_launches()
     clocks = ClockSampler(local)
     clocks.start()
@@ -273,14 +341,10 @@ def main():
     for _ in range(args.steps):
         a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         a.record()
-        _lib.check(L.sc_compress_chunks_device(h, vp(d_tok.data_ptr()), vp(d_off.data_ptr()), n_chunks,
-                                               vp(d_words.data_ptr()), cap, vp(d_woff.data_ptr()), None, sp))
-        if world > 1:
-            dist.all_gather_into_tensor(counts, d_woff[-1:].contiguous())
+        pl.compress()
+        exchange()
         b.record()
-        _lib.check(L.sc_decompress_chunks_device(h, vp(d_words.data_ptr()), vp(d_woff.data_ptr()),
-                                                 vp(d_len.data_ptr()), vp(lengths_h.ctypes.data), n_chunks,
-                                                 vp(d_back.data_ptr()), None, sp))
+        pl.decompress()
         c.record()
         torch.cuda.synchronize()
         t_comp += a.elapsed_time(b)
@@ -290,9 +354,9 @@ def main():
     clk = clocks.stop()
     elapsed_ms = ev[0].elapsed_time(ev[1])
     launches = _lib.kernel_launches() - launches0
-    prof = _lib.profile_read(h)
-    _lib.profile_enable(h, False)
-    ok = ok and bool(torch.equal(d_back[:n_tok], d_tok))
+    prof = _lib.profile_read(codec.handle)
+    _lib.profile_enable(codec.handle, False)
+    ok = ok and bool(torch.equal(pl.y, pl.x))
 
     def max_over_ranks(x):
         if world == 1:
@@ -311,32 +375,55 @@ def main():
     elapsed_max = max_over_ranks(elapsed_ms)
     t_comp_max = max_over_ranks(t_comp)
     t_dec_max = max_over_ranks(t_dec)
-    total_samples = sum_over_ranks(samples)
+    total_samples = sum_over_ranks(n_samples)
     total_stream = sum_over_ranks(stream_bytes)
     total_tokens = sum_over_ranks(n_tok)
+    total_large = sum_over_ranks(n_large)
     all_ok = sum_over_ranks(0.0 if ok else 1.0) == 0
 
-    # ---- e2e through the host entry points (pinned host buffers) -------------
+    # ---- e2e: reads from pinned host memory, record streams out and back, reads out ------
     e2e = None
     if not args.no_e2e:
-        pin_tok = torch.from_numpy(tokens).pin_memory().numpy()
-        pin_off = torch.from_numpy(offsets).pin_memory().numpy()
-        pin_words = torch.empty(cap, dtype=torch.int32).pin_memory().numpy().view(np.uint32)
-        pin_woff = torch.empty(n_chunks + 1, dtype=torch.int64).pin_memory().numpy()
-        pin_len = torch.from_numpy(lengths.astype(np.int64)).pin_memory().numpy()
-        pin_back = torch.empty(max(n_tok, 1), dtype=torch.uint8).pin_memory().numpy()
+        def pinned(n, dt):
+            return torch.empty(n, dtype=dt).pin_memory()
+
+        cap = pl.tok.numel()
+        h_x = torch.from_numpy(samples_np).pin_memory()
+        h_soff = torch.from_numpy(soff_np).pin_memory()
+        h_y = pinned(n_samples, torch.int16)
+        h_words, h_woff = pinned(pl.words.numel(), torch.int32), pinned(pl.woff.numel(), torch.int64)
+        h_large, h_pos = pinned(cap, torch.int16), pinned(cap, torch.int32)
+        h_sig0 = pinned(n_reads, torch.int16)
+        h_tokoff, h_loff = pinned(n_reads + 1, torch.int64), pinned(n_reads + 1, torch.int64)
+        moved = {"h2d": 0, "d2h": 0}
+
+        def copy(dst, src, n, kind):
+            n = src.numel() if n is None else n
+            dst[:n].copy_(src[:n], non_blocking=True)
+            moved[kind] += n * src.element_size()
 
         def host_step():
-            _lib.check(L.sc_compress_chunks(h, vp(pin_tok.ctypes.data), vp(pin_off.ctypes.data), n_chunks,
-                                            vp(pin_words.ctypes.data), cap, vp(pin_woff.ctypes.data), None, sp))
-            if world > 1:
-                counts_h = torch.tensor([int(pin_woff[-1])], dtype=torch.int64, device="cuda")
-                dist.all_gather_into_tensor(counts, counts_h)
-            _lib.check(L.sc_decompress_chunks(h, vp(pin_words.ctypes.data), vp(pin_woff.ctypes.data),
-                                              vp(pin_len.ctypes.data), n_chunks, vp(pin_back.ctypes.data), None, sp))
+            copy(pl.x, h_x, None, "h2d")
+            copy(pl.soff, h_soff, None, "h2d")
+            pl.compress()
+            exchange()
+            nw, nl, nc = int(pl.woff[pl.n_chunks].item()), int(pl.large_off[-1].item()), pl.n_chunks
+            # the record streams of the archive: words + offsets, large values, positions, sig0, offsets
+            streams = ((h_words, pl.words, nw), (h_woff, pl.woff, nc + 1), (h_large, pl.large, nl),
+                       (h_pos, pl.pos, nl), (h_sig0, pl.sig0, None), (h_tokoff, pl.tok_off, None),
+                       (h_loff, pl.large_off, None))
+            for hb, db, n in streams:
+                copy(hb, db, n, "d2h")
+            torch.cuda.current_stream().synchronize()
+            for hb, db, n in streams:
+                copy(db, hb, n, "h2d")
+            pl.decompress()
+            copy(h_y, pl.y, None, "d2h")
+            torch.cuda.current_stream().synchronize()
 
         host_step()
         sync()
+        moved = {"h2d": 0, "d2h": 0}
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(args.steps):
@@ -344,14 +431,14 @@ def main():
         e1.record()
         sync()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-        ok_e2e = bool(np.array_equal(pin_back[:n_tok], tokens))
+        ok_e2e = bool(np.array_equal(h_y.numpy(), samples_np))
         all_ok = all_ok and sum_over_ranks(0.0 if ok_e2e else 1.0) == 0
-        nw = int(pin_woff[-1])
-        h2d = tokens.nbytes + offsets.nbytes + 4 * nw + pin_woff.nbytes + pin_len.nbytes
-        d2h = 4 * nw + pin_woff.nbytes + n_chunks + n_tok + n_chunks
         e2e = {"value": round(total_samples * args.steps / (e2e_ms * 1e-3) / 1e6, 3), "unit": UNIT,
-               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-               "entry_points": "sc_compress_chunks + sc_decompress_chunks (host buffers, pinned)"}
+               "h2d_bytes_per_step": int(moved["h2d"] // args.steps),
+               "d2h_bytes_per_step": int(moved["d2h"] // args.steps),
+               "entry_points": "sc_split_signal_device + sc_compress_chunks_device | "
+                               "sc_decompress_chunks_device + sc_reassemble_signal_device; every step's reads "
+                               "and record streams through pinned host memory"}
 
     # ---- roofline of the fused kernels ------------------------------------------
     roofline = roofline_c = None
@@ -381,9 +468,9 @@ def main():
             }
 
         roofline = fused_roofline("fused_decode", "k_fused2<1>: persistent autoregressive decoder on SM pairs "
-                                                 "(9 tcgen05 int8 layers + frequency search + range decode)")
-        roofline_c = fused_roofline("fused_compress", "k_fused2<0>: fused compress on SM pairs (9 tcgen05 int8 layers "
-                                              "+ (cum, freq) selection)")
+                                                  "(9 tcgen05 int8 layers + frequency search + range decode)")
+        roofline_c = fused_roofline("fused_compress", "k_fused2<0>: fused compress on SM pairs (9 tcgen05 int8 "
+                                                      "layers + (cum, freq) selection)")
         if roofline is not None:
             roofline["kernel_ms"] = {k: round(v[0], 2) for k, v in prof.items()}
             roofline["kernel_launches"] = {k: v[1] for k, v in prof.items()}
@@ -391,10 +478,10 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n = min(args.cpu_reads, args.reads)
-        cs, ctok, coff, _ = make_batch(rank, n)
-        r = cpu_round_trip(ctok, coff, cs, steps=1, warmup=1)
+        r = cpu_round_trip(reads[:n], args.chunk_len, steps=1, warmup=1)
         cpu = {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
-               "sample": f"first {n} reads of the same batch ({cs} samples), one round trip after one warm-up",
+               "sample": f"first {n} reads of the same batch ({r['samples']} samples), one round trip after one "
+                         "warm-up",
                "compress_msps": round(r["compress"], 4), "decompress_msps": round(r["decompress"], 4)}
 
     if rank == 0:
@@ -403,16 +490,16 @@ def main():
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": "r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, "
-                                   "levels N(500,60), dwell 12, noise 12), lossless model, "
-                                   f"chunk_len {args.chunk_len}",
-                       "reads_per_gpu": args.reads, "samples_per_gpu": samples, "tokens_per_gpu": n_tok,
+            "config": {"workload": f"{WORKLOAD}, chunk_len {args.chunk_len}",
+                       "reads_per_gpu": args.reads, "samples_per_gpu": n_samples, "tokens_per_gpu": n_tok,
                        "chunks_per_gpu": n_chunks, "parallelism": f"reads sharded over {world} GPU(s)",
-                       "l2": "inputs larger than L2 (tokens per GPU > 126 MB; activations stream through HBM)"},
+                       "step": "split -> compress -> decompress -> reassemble, int16 reads in and out",
+                       "l2": "inputs larger than L2 (1.6 GB of samples per GPU); no flush needed"},
             "compress_msps": round(total_samples * args.steps / (t_comp_max * 1e-3) / 1e6, 3),
             "decompress_msps": round(total_samples * args.steps / (t_dec_max * 1e-3) / 1e6, 3),
             "bits_per_sample_neural": round(8 * total_stream / total_samples, 4),
             "bits_per_small_token": round(8 * total_stream / total_tokens, 4),
+            "large_delta_fraction": round(total_large / max(total_samples, 1), 5),
             "bit_exact_round_trip": all_ok,
             "gpu_launches": int(launches),
             "clocks": clk, "roofline": roofline, "roofline_compress": roofline_c, "cpu_baseline": cpu,
