@@ -27,7 +27,9 @@ counts (all-gather of one int64), which is how a sharded run lays out the archiv
   cpu_baseline  the CPU port of the reference codec (numpy split + int_mm GEMMs + C
              coder, oracle/) on a bounded sample, rank 0 at N=1
 
-`--impl reference` times that CPU port alone on the host cores.
+`--impl reference` times that CPU port alone on the host cores.  `--workload` picks
+another BASELINE configuration (config1: the 64-read CPU case, config3: RNA004-like
+reads, config4: the lossy mode with lsb_eliminate 3); configuration 2 is the default.
 """
 
 import argparse
@@ -48,8 +50,21 @@ UNIT = "Msamples/s"
 CHUNK_LEN = 2048
 # int8 MLP work per coded token: 2 x (8192*512 + 7*512*512 + 512*256) multiply-adds
 OPS_PER_TOKEN = 2 * (8192 * 512 + 7 * 512 * 512 + 512 * 256)
-WORKLOAD = ("r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, levels N(500,60), "
-            "dwell 12, noise 12), lossless model")
+# BASELINE.json configurations: (generator, reads, model, lossy lsb, description).  Configuration 2 is
+# the headline; 1 is the CPU-runnable case, 3 the RNA004-like set (no RNA004 model is bundled: the
+# lossless R10.4.1 model codes it), 4 the lossy mode on configuration 2's reads.
+WORKLOADS = {
+    "config1": ("r10_config1", 64, "lossless", 0,
+                "r10_config1 (64 reads x 20,000 samples, levels N(500,60), dwell 12, noise 12), lossless model"),
+    "config2": ("r10_lognormal", 20000, "lossless", 0,
+                "r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, levels N(500,60), "
+                "dwell 12, noise 12), lossless model"),
+    "config3": ("rna_lognormal", 10000, "lossless", 0,
+                "rna_lognormal (configuration 3 generator: lognormal lengths median 15,000, levels N(800,90), "
+                "dwell 30, noise 20), lossless R10.4.1 model (no RNA004 model is bundled)"),
+    "config4": ("r10_lognormal", 20000, "lossy", 3,
+                "r10_lognormal (configuration 2 reads), lossy model, lsb_eliminate 3"),
+}
 
 
 def parse_args():
@@ -58,21 +73,36 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--reads", type=int, default=20000,
-                    help="reads per GPU per step (configuration 2 is 20,000 reads)")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
+                    help="BASELINE configuration (config2, the headline, by default)")
+    ap.add_argument("--reads", type=int, default=None,
+                    help="reads per GPU per step (default: the configuration's read count)")
     ap.add_argument("--cpu-reads", type=int, default=12, help="reads in the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
                     help="tokens per chunk (2048 in every configuration; smaller values give short "
                          "decoder launches for profiling)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    gen, count, model, lsb, desc = WORKLOADS[args.workload]
+    args.generator, args.model, args.lsb, args.workload_desc = gen, model, lsb, desc
+    if args.reads is None:
+        args.reads = count
+    return args
 
 
-def make_reads(rank, n_reads):
+def lossy_round_trip(x, lsb):
+    """What SigComp's lossy mode returns for samples x (main.py:158-171, 1162-1164)."""
+    from sigcomp_b200 import signal
+    if lsb == 0:
+        return x
+    return signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(x, lsb), lsb), lsb)
+
+
+def make_reads(rank, n_reads, generator="r10_lognormal"):
     """One rank's batch of int16 reads: (reads, concatenated samples, sample offsets)."""
     from sigcomp_b200 import synthetic
-    reads = synthetic.make_reads("r10_lognormal", seed=1000 + rank, count=n_reads)
+    reads = synthetic.make_reads(generator, seed=1000 + rank, count=n_reads)
     off = np.zeros(len(reads) + 1, dtype=np.int64)
     np.cumsum([len(r) for r in reads], out=off[1:])
     return reads, np.concatenate(reads), off
@@ -157,7 +187,7 @@ def int8_peak_tops():
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
-def cpu_round_trip(reads, chunk_len, steps=1, warmup=1):
+def cpu_round_trip(reads, chunk_len, steps=1, warmup=1, lsb=0, model="lossless"):
     """The reference path ported to the CPU: numpy split / reassembly (sigcomp_b200.signal,
     pinned to the reference's outputs) around the oracle codec (int_mm GEMMs + C coder)."""
     import torch
@@ -166,12 +196,14 @@ def cpu_round_trip(reads, chunk_len, steps=1, warmup=1):
     from sigcomp_b200.model import load_model
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    om = OracleModel(load_model(name="lossless"))
+    om = OracleModel(load_model(name=model))
     samples = int(sum(len(r) for r in reads))
+    want = [lossy_round_trip(r, lsb) for r in reads]
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        splits = [signal.split_signal(r) for r in reads]
+        splits = [signal.split_signal(signal.lossy_encode(signal.reduce_lsb(r, lsb), lsb) if lsb else r)
+                  for r in reads]
         chunks = [sp[1][j:j + chunk_len] for sp in splits for j in range(0, len(sp[1]), chunk_len)]
         streams = om.compress_chunks(chunks, chunk_len=chunk_len, backend="int_mm")
         t1 = time.perf_counter()
@@ -181,11 +213,12 @@ def cpu_round_trip(reads, chunk_len, steps=1, warmup=1):
             k = (len(sp[1]) + chunk_len - 1) // chunk_len
             tok = np.concatenate(back[pos:pos + k]) if k else np.zeros(0, np.uint8)
             pos += k
-            out.append(signal.reassemble_signal(sp[0], len(r), tok, sp[2], sp[3]))
+            sig = signal.reassemble_signal(sp[0], len(r), tok, sp[2], sp[3])
+            out.append(signal.lossy_decode(sig, lsb) if lsb else sig)
         t2 = time.perf_counter()
         if i >= warmup:
             times.append((t1 - t0, t2 - t1))
-        assert all(np.array_equal(a, b) for a, b in zip(out, reads))
+        assert all(np.array_equal(a, b) for a, b in zip(out, want))
     tc = sum(t[0] for t in times) / len(times)
     td = sum(t[1] for t in times) / len(times)
     return {"value": samples / (tc + td) / 1e6, "compress": samples / tc / 1e6, "decompress": samples / td / 1e6,
@@ -197,15 +230,15 @@ def run_reference(args):
     if rank != 0:
         return 0
     n_reads = args.cpu_reads
-    reads, _, _ = make_reads(0, n_reads)
-    r = cpu_round_trip(reads, args.chunk_len, steps=args.steps, warmup=args.warmup)
-    sample = f"{n_reads} reads ({r['samples']} samples) of the configuration-2 generator per step"
+    reads, _, _ = make_reads(0, n_reads, args.generator)
+    r = cpu_round_trip(reads, args.chunk_len, steps=args.steps, warmup=args.warmup, lsb=args.lsb, model=args.model)
+    sample = f"{n_reads} reads ({r['samples']} samples) of the {args.workload} generator per step"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(r["seconds_per_step"] * 1e3, 1), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": f"{WORKLOAD}, chunk_len {args.chunk_len}", "reads_per_step": n_reads,
+        "config": {"workload": f"{args.workload_desc}, chunk_len {args.chunk_len}", "reads_per_step": n_reads,
                    "samples_per_step": r["samples"]},
         "compress_msps": round(r["compress"], 4), "decompress_msps": round(r["decompress"], 4),
         "cpu_baseline": {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
@@ -219,12 +252,12 @@ def run_reference(args):
 class Pipeline:
     """Device buffers and the C-ABI calls of one rank's round trip."""
 
-    def __init__(self, codec, n_reads, n_samples, chunk_len):
+    def __init__(self, codec, n_reads, n_samples, chunk_len, lsb=0):
         import ctypes
         import torch
         self.torch, self.vp = torch, ctypes.c_void_p
         self.L, self.h = codec._lib, codec.handle
-        self.chunk_len = chunk_len
+        self.chunk_len, self.lsb = chunk_len, lsb
         self.R, self.S = n_reads, n_samples
         dev = torch.device("cuda", torch.cuda.current_device())
         cap = max(n_samples - n_reads, 1)
@@ -254,7 +287,7 @@ class Pipeline:
     def compress(self):
         from sigcomp_b200 import _lib
         L, h, p, sp = self.L, self.h, self.p, self.vp(self.stream.cuda_stream)
-        _lib.check(L.sc_split_signal_device(h, p(self.x), p(self.soff), self.R, 0, p(self.sig0), p(self.tok),
+        _lib.check(L.sc_split_signal_device(h, p(self.x), p(self.soff), self.R, self.lsb, p(self.sig0), p(self.tok),
                                             p(self.tok_off), p(self.large), p(self.pos), p(self.large_off), sp))
         # chunk boundaries of the per-read token streams (host, from the R + 1 token offsets)
         choff = chunk_offsets(self.tok_off.cpu().numpy(), self.chunk_len)
@@ -272,7 +305,7 @@ class Pipeline:
         _lib.check(L.sc_decompress_chunks_device(h, p(self.words), p(self.woff), p(self.chlen),
                                                  self.vp(self.chlen_h.ctypes.data), self.n_chunks, p(self.tok2),
                                                  None, sp))
-        _lib.check(L.sc_reassemble_signal_device(h, p(self.sig0), p(self.soff), self.R, 0, p(self.tok2),
+        _lib.check(L.sc_reassemble_signal_device(h, p(self.sig0), p(self.soff), self.R, self.lsb, p(self.tok2),
                                                  p(self.tok_off), p(self.large), p(self.pos), p(self.large_off),
                                                  p(self.y), sp))
 
@@ -296,10 +329,11 @@ def main():
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    reads, samples_np, soff_np = make_reads(rank, args.reads)
+    reads, samples_np, soff_np = make_reads(rank, args.reads, args.generator)
     n_reads, n_samples = len(reads), int(soff_np[-1])
-    codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name="lossless"))
-    pl = Pipeline(codec, n_reads, n_samples, args.chunk_len)
+    codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name=args.model))
+    pl = Pipeline(codec, n_reads, n_samples, args.chunk_len, args.lsb)
+    want = torch.from_numpy(lossy_round_trip(samples_np, args.lsb)).cuda()   # what the round trip must return
     pl.x.copy_(torch.from_numpy(samples_np))
     pl.soff.copy_(torch.from_numpy(soff_np))
     counts = torch.zeros(world, dtype=torch.int64, device="cuda")
@@ -321,7 +355,7 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    ok = bool(torch.equal(pl.y, pl.x))
+    ok = bool(torch.equal(pl.y, want))
     n_tok = int(pl.tok_off[-1].item())
     n_large = int(pl.large_off[-1].item())
     n_chunks = pl.n_chunks
@@ -356,7 +390,7 @@ def main():
     launches = _lib.kernel_launches() - launches0
     prof = _lib.profile_read(codec.handle)
     _lib.profile_enable(codec.handle, False)
-    ok = ok and bool(torch.equal(pl.y, pl.x))
+    ok = ok and bool(torch.equal(pl.y, want))
 
     def max_over_ranks(x):
         if world == 1:
@@ -431,7 +465,7 @@ def main():
         e1.record()
         sync()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-        ok_e2e = bool(np.array_equal(h_y.numpy(), samples_np))
+        ok_e2e = bool(np.array_equal(h_y.numpy(), want.cpu().numpy()))
         all_ok = all_ok and sum_over_ranks(0.0 if ok_e2e else 1.0) == 0
         e2e = {"value": round(total_samples * args.steps / (e2e_ms * 1e-3) / 1e6, 3), "unit": UNIT,
                "h2d_bytes_per_step": int(moved["h2d"] // args.steps),
@@ -478,7 +512,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         n = min(args.cpu_reads, args.reads)
-        r = cpu_round_trip(reads[:n], args.chunk_len, steps=1, warmup=1)
+        r = cpu_round_trip(reads[:n], args.chunk_len, steps=1, warmup=1, lsb=args.lsb, model=args.model)
         cpu = {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
                "sample": f"first {n} reads of the same batch ({r['samples']} samples), one round trip after one "
                          "warm-up",
@@ -490,7 +524,7 @@ def main():
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps, 2), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-            "config": {"workload": f"{WORKLOAD}, chunk_len {args.chunk_len}",
+            "config": {"workload": f"{args.workload_desc}, chunk_len {args.chunk_len}",
                        "reads_per_gpu": args.reads, "samples_per_gpu": n_samples, "tokens_per_gpu": n_tok,
                        "chunks_per_gpu": n_chunks, "parallelism": f"reads sharded over {world} GPU(s)",
                        "step": "split -> compress -> decompress -> reassemble, int16 reads in and out",
