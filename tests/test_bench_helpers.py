@@ -1,0 +1,44 @@
+"""Host logic of bench.py: chunking of per-read token streams and the
+configuration table (CPU only)."""
+
+import numpy as np
+
+import bench
+
+
+def test_chunk_offsets_cut_each_read_into_chunk_len_pieces():
+    tok_off = np.array([0, 5000, 5000, 9000, 13097], dtype=np.int64)
+    got = bench.chunk_offsets(tok_off, 2048)
+    assert got.tolist() == [0, 2048, 4096, 5000, 7048, 9000, 11048, 13096, 13097]
+
+
+def test_chunk_offsets_match_sigcomp_framing():
+    # ReadFramingMixin cuts every read's tokens into chunk_len pieces (cpu_compression.py:28-50)
+    rng = np.random.default_rng(4)
+    lens = rng.integers(0, 9000, size=50)
+    tok_off = np.zeros(51, dtype=np.int64)
+    np.cumsum(lens, out=tok_off[1:])
+    want = []
+    for r in range(50):
+        want += list(range(int(tok_off[r]), int(tok_off[r + 1]), 1024))
+    want.append(int(tok_off[-1]))
+    assert bench.chunk_offsets(tok_off, 1024).tolist() == want
+
+
+def test_chunk_offsets_empty():
+    assert bench.chunk_offsets(np.array([0], dtype=np.int64), 2048).tolist() == [0]
+
+
+def test_workloads_cover_baseline_configurations():
+    assert set(bench.WORKLOADS) == {"config1", "config2", "config3", "config4"}
+    assert bench.WORKLOADS["config2"][:4] == ("r10_lognormal", 20000, "lossless", 0)
+    assert bench.WORKLOADS["config4"][2:4] == ("lossy", 3)
+
+
+def test_lossy_round_trip_matches_signal_module():
+    from sigcomp_b200 import signal
+    x = np.asarray([0, 1, 7, 8, 9, -5, 32767, -32768, 1234], dtype=np.int16)
+    assert np.array_equal(bench.lossy_round_trip(x, 0), x)
+    y = bench.lossy_round_trip(x, 3)
+    assert np.array_equal(y, signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(x, 3), 3), 3))
+    assert np.all(np.abs(y.astype(np.int32) - x.astype(np.int32))[:6] <= 4)
