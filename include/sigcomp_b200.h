@@ -170,6 +170,16 @@ SC_API int sc_reassemble_signal_device(sc_model *model, const int16_t *sig0, con
                                        int16_t *samples, void *stream);
 
 /*
+ * Failure-detection self test (no counterpart in the reference, which has no
+ * device-side waits).  Every device-side wait in this library is bounded: after
+ * its time limit (2 s) the kernel records the timeout in a device error flag and
+ * returns, and the API call reports SC_ERR_CUDA ("a device-side wait timed out").
+ * This call runs one small kernel whose waits nothing will satisfy, so it returns
+ * SC_ERR_CUDA with that message after about 4 s; the device stays usable.
+ */
+SC_API int sc_selftest_wait_timeout(sc_model *model, void *stream);
+
+/*
  * sc_mlp_logits_device without any device allocation.  No counterpart in the
  * reference: it exists for callers that cannot call cudaMalloc, such as a host
  * framework that has reserved the GPU's memory for its own pool, or a

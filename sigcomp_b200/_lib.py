@@ -23,7 +23,7 @@ EXPORTS = (
     "sc_model_set_mlp_path", "sc_compress_chunks", "sc_compress_chunks_device", "sc_decompress_chunks",
     "sc_decompress_chunks_device", "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read",
     "sc_trace_enable", "sc_trace_read", "sc_mlp_logits_device_noalloc", "sc_split_signal_device",
-    "sc_reassemble_signal_device",
+    "sc_reassemble_signal_device", "sc_selftest_wait_timeout",
 )
 
 KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step",
@@ -68,7 +68,8 @@ def load():
     for name in ("sc_model_create", "sc_model_destroy", "sc_model_set_mlp_path", "sc_compress_chunks",
                  "sc_compress_chunks_device", "sc_decompress_chunks", "sc_decompress_chunks_device",
                  "sc_mlp_logits_device", "sc_mlp_logits_device_noalloc", "sc_profile_enable",
-                 "sc_profile_read", "sc_split_signal_device", "sc_reassemble_signal_device"):
+                 "sc_profile_read", "sc_split_signal_device", "sc_reassemble_signal_device",
+                 "sc_selftest_wait_timeout"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L

@@ -33,6 +33,7 @@ void run_mlp(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, 
 int split_signal_device(sc_model *m, const int16_t *samples, const int64_t *off_d, const int64_t *off_h,
                         int64_t n_reads, int lsb, int16_t *sig0, uint8_t *small, int64_t *small_off,
                         uint16_t *large, uint32_t *large_pos, int64_t *large_off, cudaStream_t s);
+int wait_selftest(cudaStream_t s, int *done_d);
 int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *off_d, int64_t n_reads, int lsb,
                              const uint8_t *small, const int64_t *small_off, const uint16_t *large,
                              const uint32_t *large_pos, const int64_t *large_off, int16_t *samples,
@@ -477,6 +478,26 @@ int64_t sc_trace_read(sc_model *m, int32_t cta, uint64_t *records, int64_t capac
         return SC_OK;
     });
     return rc == SC_OK ? n : -1;
+}
+
+int sc_selftest_wait_timeout(sc_model *m, void *stream)
+{
+    g_err[0] = 0;
+    if (!m) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        int *done = (int *)m->ws_misc.get(64, s);
+        SC_CUDA(cudaMemsetAsync(done, 0, sizeof(int), s));
+        const int r = wait_selftest(s, done);
+        if (r != 4) {                    // the kernel must end, with both waits timed out
+            set_error("wait self test: unexpected result %d", r);
+            return SC_ERR_CUDA;
+        }
+        return SC_OK;                    // guarded() reports the recorded timeout
+    });
 }
 
 // read offsets of a signal call: nondecreasing, every read at least one sample

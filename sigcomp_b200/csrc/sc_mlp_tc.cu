@@ -616,6 +616,41 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
     count_launch();
 }
 
+namespace {
+
+// Failure-detection self test: one warp waits on an mbarrier and on a shared-memory
+// counter that nothing signals.  Both waits give up after their time limit, record
+// the timeout in the device error flag and return, so the kernel ends normally.
+__global__ void k_wait_selftest(int *done)
+{
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ uint32_t cnt;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        cnt = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const bool a = mbar_wait(&bar, 0);          // no arrival ever comes
+        const bool b = counter_wait(&cnt, 1);       // no increment ever comes
+        *done = (a ? 1 : 0) | (b ? 2 : 0) | 4;
+    }
+}
+
+}  // namespace
+
+int wait_selftest(cudaStream_t s, int *done_d)
+{
+    k_wait_selftest<<<1, 32, 0, s>>>(done_d);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    int done = 0;
+    SC_CUDA(cudaMemcpyAsync(&done, done_d, sizeof(int), cudaMemcpyDeviceToHost, s));
+    SC_CUDA(cudaStreamSynchronize(s));
+    return done;
+}
+
 int read_device_error(int clear)
 {
     int v = 0;

@@ -95,3 +95,37 @@ def test_sharded_compress_reassembles_single_process_output(tmp_path, world, n_r
     assert seen[0][0] == 0 and max(s[1] for s in seen) == n_reads
     if n_reads < world:   # ranks without reads still join the exchange, with an empty shard
         assert seen[-1][0] == seen[-1][1] == n_reads
+
+
+def _rank_dies_main(rank, world, port, out_dir):
+    """Rank 1 leaves before the byte-count exchange; rank 0 must get an error, not hang."""
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=10))
+    if rank == 1:
+        os._exit(0)                       # dies without taking part in the collective
+    try:
+        compress_shard(_FakeCodec(), _reads(7), rank=rank, world=world)
+        outcome = "completed"
+    except Exception as e:                # gloo reports the lost peer or the timeout
+        outcome = "error: " + type(e).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(outcome)
+    os._exit(0)
+
+
+def test_lost_rank_is_reported_to_the_others(tmp_path):
+    import torch.multiprocessing as mp
+    ctx = mp.start_processes(_rank_dies_main, args=(2, _free_port(), str(tmp_path)), nprocs=2,
+                             start_method="spawn", join=False)
+    import time
+    deadline = time.time() + 120
+    while not ctx.join(timeout=5) and time.time() < deadline:
+        pass
+    for p in ctx.processes:
+        if p.is_alive():
+            p.kill()
+    outcome = (tmp_path / "rank0.txt").read_text()
+    assert outcome.startswith("error"), outcome
