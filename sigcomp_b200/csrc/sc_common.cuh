@@ -125,10 +125,13 @@ __device__ __forceinline__ RowDivisor make_row_divisor(uint64_t T) {
 }
 
 __device__ __forceinline__ uint32_t div_freq(uint64_t w, const RowDivisor &d) {
-    uint64_t q = (w * d.R) >> 38;
-    const uint64_t r = (w << 24) - q * d.T;
+    // floor(w * R / 2^38) in 32-bit pieces: w = wh * 2^32 + wl (wh <= 64), R < 2^25, so
+    // floor(w * R / 2^32) = wh * R + mulhi(wl, R) < 2^31 exactly; one more shift by 6.
+    const uint32_t wl = (uint32_t)w, wh = (uint32_t)(w >> 32), R = (uint32_t)d.R;
+    uint32_t q = (wh * R + __umulhi(wl, R)) >> 6;
+    const uint64_t r = (w << 24) - (uint64_t)q * d.T;   // true remainder in [0, 2T), mod 2^64
     q += (r >= d.T) ? 1u : 0u;
-    return (uint32_t)q;
+    return q;
 }
 
 // ---------------------------------------------------------------------------

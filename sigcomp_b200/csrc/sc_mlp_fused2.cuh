@@ -112,21 +112,28 @@ __device__ __forceinline__ void trace_ev(const Fused2Params &p, int role, int ev
 // packed logits in TMEM (64 words from taddr) with the maximum logit m known:
 // row divisor, fix-up amount, first index of the maximum frequency and, for
 // sym >= 0, the exclusive cumulative frequency and frequency of sym.
+// With CACHE_F, the frequencies of symbols 0..191 (before the fix-up) are also
+// stored in TMEM columns 64..255 of the same accumulator (read already), where
+// row_find_cached picks them up instead of recomputing them.
+template <bool CACHE_F = false>
 __device__ __forceinline__ void row_stats(uint32_t taddr, const uint64_t *lut_s, int m, RowDivisor &d, uint32_t &fix,
                                           int &amax, int sym, uint32_t &sym_cum, uint32_t &sym_f)
 {
-    uint64_t T = 0;
+    uint64_t T0 = 0, T1 = 0;                         // two chains of 64-bit adds
 #pragma unroll 1
     for (int g = 0; g < 4; ++g) {
         uint32_t w[16];
         tmem_ld16(taddr + g * 16, w);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < 16; i += 2)
 #pragma unroll
-            for (int b = 0; b < 4; ++b) T += lut_s[m - pk_get(w[i], b)];
+            for (int b = 0; b < 4; ++b) {
+                T0 += lut_s[m - pk_get(w[i], b)];
+                T1 += lut_s[m - pk_get(w[i + 1], b)];
+            }
     }
-    d = make_row_divisor(T);
+    d = make_row_divisor(T0 + T1);
     uint32_t total = 0, best = 0, below = 0, fsym = 0;
     amax = 0;
 #pragma unroll 1
@@ -134,6 +141,7 @@ __device__ __forceinline__ void row_stats(uint32_t taddr, const uint64_t *lut_s,
         uint32_t w[16];
         tmem_ld16(taddr + g * 16, w);
         tmem_ld_wait();
+        uint32_t f8[8];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
 #pragma unroll
@@ -145,11 +153,72 @@ __device__ __forceinline__ void row_stats(uint32_t taddr, const uint64_t *lut_s,
                 if (f > best) { best = f; amax = v; }
                 below += v < sym ? f : 0u;
                 fsym = v == sym ? f : fsym;
+                if (CACHE_F) {
+                    f8[(4 * i + b) & 7] = f;
+                    if (((4 * i + b) & 7) == 7 && g < 3) tmem_st8(taddr + 64 + g * 64 + 4 * i + b - 7, f8);
+                }
             }
     }
+    if (CACHE_F) tmem_st_wait();
     fix = total - SC_TOTAL;          // modulo 2^32; subtracting it from f[amax] is exact
     sym_cum = below - (amax < sym ? fix : 0u);
     sym_f = fsym - (amax == sym ? fix : 0u);
+}
+
+// row_find with the frequencies of symbols 0..191 read back from TMEM (row_stats<true>)
+__device__ __forceinline__ void row_find_cached(uint32_t taddr, const uint64_t *lut_s, int m, const RowDivisor &d,
+                                                uint32_t fix, int amax, uint32_t q, int &sym, uint32_t &sym_cum,
+                                                uint32_t &sym_f)
+{
+    uint32_t cum = 0;
+    bool found = false;
+    sym = SC_VOCAB - 1;
+    sym_cum = 0;
+    sym_f = 0;
+#pragma unroll 1
+    for (int g = 0; g < 4; ++g) {
+        if (!__any_sync(0xffffffffu, !found)) break;
+        if (g < 3) {
+#pragma unroll 1
+            for (int c4 = 0; c4 < 4; ++c4) {
+                uint32_t fv[16];
+                tmem_ld16(taddr + 64 + g * 64 + c4 * 16, fv);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int v = g * 64 + c4 * 16 + j;
+                    const uint32_t f = fv[j] - (v == amax ? fix : 0u);
+                    if (!found && cum + f > q) {
+                        found = true;
+                        sym = v;
+                        sym_cum = cum;
+                        sym_f = f;
+                    }
+                    cum += f;
+                }
+            }
+        } else {
+            uint32_t w[16];
+            tmem_ld16(taddr + g * 16, w);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) {
+                    const int v = g * 64 + 4 * i + b;
+                    uint32_t f = div_freq(lut_s[m - pk_get(w[i], b)], d);
+                    f = f < 1u ? 1u : f;
+                    f -= v == amax ? fix : 0u;
+                    if (!found && cum + f > q) {
+                        found = true;
+                        sym = v;
+                        sym_cum = cum;
+                        sym_f = f;
+                    }
+                    cum += f;
+                }
+        }
+    }
 }
 
 // The symbol whose cumulative interval holds q: the first v with cum_v + f_v > q.
@@ -497,8 +566,8 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     int amax, sym;
                     RowDivisor d;
                     uint32_t fix, cum, f;
-                    row_stats(taddr, lut_s, mlogit, d, fix, amax, -1, cum, f);
-                    row_find(taddr, lut_s, mlogit, d, fix, amax, dlive ? (uint32_t)dq : 0u, sym, cum, f);
+                    row_stats<true>(taddr, lut_s, mlogit, d, fix, amax, -1, cum, f);
+                    row_find_cached(taddr, lut_s, mlogit, d, fix, amax, dlive ? (uint32_t)dq : 0u, sym, cum, f);
                     if (dlive) {
                         DecState s = ds;
                         s.lower += dscale * (uint64_t)cum;
