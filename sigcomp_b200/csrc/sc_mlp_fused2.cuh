@@ -165,7 +165,10 @@ __device__ __forceinline__ void row_stats(uint32_t taddr, const uint64_t *lut_s,
     sym_f = fsym - (amax == sym ? fix : 0u);
 }
 
-// row_find with the frequencies of symbols 0..191 read back from TMEM (row_stats<true>)
+// The symbol whose fixed-up cumulative interval holds q: the first v with cum_v + f_v > q,
+// with the frequencies of symbols 0..191 read back from TMEM (row_stats<true>) and those
+// of 192..255 recomputed.  The warp scans groups while any lane is still searching (the
+// TMEM loads are warp-collective).
 __device__ __forceinline__ void row_find_cached(uint32_t taddr, const uint64_t *lut_s, int m, const RowDivisor &d,
                                                 uint32_t fix, int amax, uint32_t q, int &sym, uint32_t &sym_cum,
                                                 uint32_t &sym_f)
@@ -218,43 +221,6 @@ __device__ __forceinline__ void row_find_cached(uint32_t taddr, const uint64_t *
                     cum += f;
                 }
         }
-    }
-}
-
-// The symbol whose cumulative interval holds q: the first v with cum_v + f_v > q.
-// Groups of 64 symbols are scanned only while a lane of the warp is still
-// searching (the TMEM loads are warp-collective).
-__device__ __forceinline__ void row_find(uint32_t taddr, const uint64_t *lut_s, int m, const RowDivisor &d,
-                                         uint32_t fix, int amax, uint32_t q, int &sym, uint32_t &sym_cum,
-                                         uint32_t &sym_f)
-{
-    uint32_t cum = 0;
-    bool found = false;
-    sym = SC_VOCAB - 1;
-    sym_cum = 0;
-    sym_f = 0;
-#pragma unroll 1
-    for (int g = 0; g < 4; ++g) {
-        if (!__any_sync(0xffffffffu, !found)) break;
-        uint32_t w[16];
-        tmem_ld16(taddr + g * 16, w);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int v = g * 64 + 4 * i + b;
-                uint32_t f = div_freq(lut_s[m - pk_get(w[i], b)], d);
-                f = f < 1u ? 1u : f;
-                f -= v == amax ? fix : 0u;
-                if (!found && cum + f > q) {
-                    found = true;
-                    sym = v;
-                    sym_cum = cum;
-                    sym_f = f;
-                }
-                cum += f;
-            }
     }
 }
 
