@@ -26,7 +26,10 @@
 
 namespace sc {
 
-constexpr int KT2 = 5;                // pair-tiles in flight per CTA pair
+// pair-tiles in flight per CTA pair: six for the decoder (more units to overlap its
+// long last-layer epilogues), five for compression (smaller activation buffers in L2)
+constexpr int KT2 = 6;                // the larger of the two: sizes per-slot arrays
+template <bool DECODE> constexpr int kt2() { return DECODE ? 6 : 5; }
 
 struct Fused2Params {
     CUtensorMap w[FMAX_LAYERS];       // weights, box 128 rows x 128 B (half of a 256-row unit)
@@ -53,7 +56,7 @@ struct Fused2Params {
     uint2 *pairs;
     // decode
     CUtensorMap ering;                // embedding ring, box 128 rows x 128 B
-    int8_t *ering_ptr;                // [grid][KT2][WIN][TM][128], then the start-of-sequence block
+    int8_t *ering_ptr;                // [grid][kt2][WIN][TM][128], then the start-of-sequence block
     int64_t ering_sos_row;            // first row of the start-of-sequence block
     const int64_t *order;
     int64_t n_rows;
@@ -234,8 +237,9 @@ __device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
     const int n_pt = (p.n_tiles + 1) / 2;
     const int my_pt = n_pt > pair ? (n_pt - 1 - pair) / NP + 1 : 0;
     const int NL = p.num_layers;
-    for (int g0 = 0, grp = 0; g0 < my_pt; g0 += KT2, ++grp) {
-        const int gn = min(KT2, my_pt - g0);
+    constexpr int KTD = kt2<DECODE>();
+    for (int g0 = 0, grp = 0; g0 < my_pt; g0 += KTD, ++grp) {
+        const int gn = min(KTD, my_pt - g0);
         int maxlen[KT2];
         int steps = 1;
 #pragma unroll
@@ -315,7 +319,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
     cluster_sync();                       // both CTAs' barriers exist before any remote use
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int slot_row0 = blockIdx.x * KT2 * TM;
+    const int slot_row0 = blockIdx.x * kt2<DECODE>() * TM;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -335,7 +339,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return false;
                 }
                 trace_ev(p, 0, 1, L, nh, tt, step);
-                const int ring0 = (blockIdx.x * KT2 + tt) * WIN * TM;
+                const int ring0 = (blockIdx.x * kt2<DECODE>() + tt) * WIN * TM;
                 // compress layer 0 reads A from the sliding buffer: its stages carry the
                 // weights of two K blocks (the second in the unused activation half)
                 const int kstep = (!DECODE && L == 0) ? 2 : 1;
@@ -550,7 +554,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                         // append the token's embedding row to this row's window ring
                         const int4 *e = reinterpret_cast<const int4 *>(p.emb + sym * EMB_DIM);
                         int4 *dst = reinterpret_cast<int4 *>(
-                            p.ering_ptr + (((size_t)(blockIdx.x * KT2 + tt) * WIN + (step & (WIN - 1))) * TM + r) * KB);
+                            p.ering_ptr + (((size_t)(blockIdx.x * kt2<DECODE>() + tt) * WIN + (step & (WIN - 1))) * TM + r) * KB);
 #pragma unroll
                         for (int i = 0; i < KB / 16; ++i) dst[i] = e[i];
                     }

@@ -471,12 +471,12 @@ static bool use_pairs(const sc_model *m) { return m->mlp_path != 4 && m->num_sms
 
 int64_t fused_decode_capacity(const sc_model *m)
 {
-    return use_pairs(m) ? (int64_t)(m->num_sms / 2) * KT2 * 2 * TM : (int64_t)m->num_sms * KT * TM;
+    return use_pairs(m) ? (int64_t)(m->num_sms / 2) * kt2<true>() * 2 * TM : (int64_t)m->num_sms * KT * TM;
 }
 
 static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s)
 {
-    const int64_t rows = (int64_t)grid * KT2 * TM;
+    const int64_t rows = (int64_t)grid * KT2 * TM;      // enough for either kernel's slots
     int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
     int8_t *a1 = (int8_t *)m->ws_act1.get((size_t)rows * MAX_N, s);
     p.act_ptr[0] = a0;
@@ -572,11 +572,12 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
     if (use_pairs(m)) {
         const int64_t n_pt = (n_tiles + 1) / 2;
         const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);
-        if (n_pt > (int64_t)(grid / 2) * KT2) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        if (n_pt > (int64_t)(grid / 2) * kt2<true>())
+            throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
         Fused2Params p{};
         fused2_common(m, p, grid, s);
-        // embedding ring: [grid][KT2][WIN] blocks of 128 rows x 128 B, then the SOS block
-        const int64_t ring_rows = (int64_t)grid * KT2 * WIN * TM;
+        // embedding ring: [grid][kt2][WIN] blocks of 128 rows x 128 B, then the SOS block
+        const int64_t ring_rows = (int64_t)grid * kt2<true>() * WIN * TM;
         int8_t *ring = (int8_t *)m->ws_ering.get((size_t)(ring_rows + TM) * KB, s);
         k_sos_block<<<1, TM * KB / 16, 0, s>>>(ring + ring_rows * KB, m->emb);
         SC_LAUNCH_CHECK();
