@@ -19,6 +19,9 @@ Fixtures written:
   signal.npz       - reference _split_signal / lossy transform outputs
   sharding.json    - sample counts -> read ranges of the reference multi-GPU partition
                      (sigcomp/read_assignment.py); `--only sharding` rewrites just this file
+  records.npz      - read records written by the reference's _write_read_payload and the SIDX
+                     index entries (sigcomp/main.py:549-590, archive_shards.py:22);
+                     `--only records` rewrites just this file
 """
 
 import argparse
@@ -102,6 +105,57 @@ def _encode_reference(ce, lut, logits, symbols, backend):
     return enc.get_compressed()[0], saw_inversion
 
 
+def _record_cases(path):
+    """A batch of read records through the reference writer, parser and index entry format."""
+    import io
+    cc, ce, ci, sm = _import_reference(path)
+    import sigcomp.archive_shards as ash
+    rng = np.random.default_rng(11)
+    recs, meta, blobs = [], [], []
+    buf = io.BytesIO()
+    for i in range(40):
+        rec = sm.REC_FMT.pack(rng.bytes(16), float(rng.random()), float(rng.normal()), int(rng.integers(0, 256)),
+                              int(rng.integers(0, 256)), float(rng.random() * 5000), int(rng.integers(0, 2 ** 32)),
+                              int(rng.integers(0, 2 ** 32)), int(rng.integers(0, 2 ** 32)), int(rng.integers(0, 2 ** 62)))
+        n = int(rng.integers(1, 100000))
+        c_small = int(rng.integers(0, n))
+        sizes = [0 if i % 7 == 0 else int(rng.integers(0, 400)) for _ in range(3)]
+        s_b, l_b, p_b = (rng.bytes(k) for k in sizes)
+        sig0 = int(rng.integers(-32768, 32768))
+        sm._write_read_payload(buf, rec, sig0, n, c_small, s_b, l_b, p_b)
+        recs.append(rec)
+        meta.append((sig0, n, c_small))
+        blobs.append((s_b, l_b, p_b))
+    region = buf.getvalue()
+    # parse back with the reference reader
+    rd = io.BytesIO(region)
+    parsed = []
+    while True:
+        item = sm._parse_read_payload(rd)
+        if item is None:
+            break
+        info, split = item
+        parsed.append((split["sig0"], split["N"], split["c_small"], split["c_large"]))
+    assert len(parsed) == 40
+    ids = [r[:16] for r in recs]
+    offsets = np.cumsum([0] + [len(r) + sm.SPLIT_HDR_FMT.size + 12 + sum(len(x) for x in b)
+                               for r, b in zip(recs, blobs)])[:-1]
+    index = ash.IDX_MAGIC + sm.U32.pack(40) + b"".join(ash.INDEX_ENTRY.pack(i_, 1000 + int(o)) for i_, o in zip(ids, offsets))
+
+    def cat(parts):
+        return np.frombuffer(b"".join(parts), dtype=np.uint8), np.cumsum([0] + [len(p_) for p_ in parts]).astype(np.int64)
+
+    rec_flat, rec_off = cat(recs)
+    s_flat, s_off = cat([b[0] for b in blobs])
+    l_flat, l_off = cat([b[1] for b in blobs])
+    p_flat, p_off = cat([b[2] for b in blobs])
+    np.savez_compressed(HERE / "records.npz", region=np.frombuffer(region, dtype=np.uint8),
+                        rec=rec_flat, rec_off=rec_off, meta=np.asarray(meta, dtype=np.int64),
+                        s=s_flat, s_off=s_off, l=l_flat, l_off=l_off, p=p_flat, p_off=p_off,
+                        parsed=np.asarray(parsed, dtype=np.int64), index=np.frombuffer(index, dtype=np.uint8),
+                        index_base=np.asarray([1000]))
+
+
 def _sharding_cases(path):
     """Read ranges of sample_balanced_ranges for edge cases and synthetic read sets."""
     sys.path.insert(0, str(path))
@@ -135,11 +189,14 @@ def _sharding_cases(path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["sharding"], default=None)
+    ap.add_argument("--only", choices=["sharding", "records"], default=None)
     args = ap.parse_args()
     os.environ.setdefault("NUMBA_CACHE_DIR", "/tmp/nbcache")
-    _sharding_cases(Path(args.reference))
-    if args.only == "sharding":
+    if args.only in (None, "sharding"):
+        _sharding_cases(Path(args.reference))
+    if args.only in (None, "records"):
+        _record_cases(Path(args.reference))
+    if args.only is not None:
         return
     cc, ce, ci, sm = _import_reference(Path(args.reference))
     sys.path.insert(0, str(REPO))
