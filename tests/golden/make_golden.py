@@ -19,6 +19,8 @@ Fixtures written:
   signal.npz       - reference _split_signal / lossy transform outputs
   sharding.json    - sample counts -> read ranges of the reference multi-GPU partition
                      (sigcomp/read_assignment.py); `--only sharding` rewrites just this file
+  streams_rna.npz  - RNA004-like reads (configuration 3 generator) through the reference CPU codec
+                     with the lossless model; `--only rna` rewrites just this file
   records.npz      - read records written by the reference's _write_read_payload and the SIDX
                      index entries (sigcomp/main.py:549-590, archive_shards.py:22);
                      `--only records` rewrites just this file
@@ -156,6 +158,38 @@ def _record_cases(path):
                         index_base=np.asarray([1000]))
 
 
+def _rna_streams(path):
+    """Configuration-3-like reads (levels N(800, 90), dwell 30, noise 20: more large deltas) through
+    the reference CPU codec with the lossless model (no RNA004 model is bundled)."""
+    cc, ce, ci, sm = _import_reference(path)
+    sys.path.insert(0, str(REPO))
+    from sigcomp_b200 import synthetic
+    model_dir = Path(path) / "sigcomp" / "pretrained_models"
+    codec = cc.CPUQuantMLPCompression(chunk_len=2048, model_path=str(model_dir / "lossless.pth"),
+                                      inference_backend="int_mm", epilogue="numba", inference_batch_size=4096)
+    rng = np.random.default_rng(33)
+    reads = [synthetic.synth_read(rng, n, synthetic.RNA004) for n in (6000, 2500, 700, 2)]
+    token_reads = [sm._split_signal(s)[1] for s in reads]
+    chunks = []
+    for tr in token_reads:
+        chunks.extend(tr[i:i + 2048] for i in range(0, len(tr), 2048))
+    streams = codec.compress_chunks(chunks, max_batch_size=1024)
+    lengths = [len(c) for c in chunks]
+    back = codec.decompress_chunks(streams, lengths, max_batch_size=4096)
+    assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+    framed = codec.batch_inference_reads(list_of_reads=token_reads, batch_size=1024)
+    tok = np.concatenate([np.asarray(c, np.uint8) for c in chunks])
+    np.savez_compressed(
+        HERE / "streams_rna.npz", tokens=tok, offsets=np.cumsum([0] + lengths).astype(np.int64),
+        words=np.frombuffer(b"".join(streams), dtype="<u4"),
+        word_offsets=np.cumsum([0] + [len(x) // 4 for x in streams]).astype(np.int64),
+        read_tokens=np.concatenate(token_reads),
+        read_offsets=np.cumsum([0] + [len(t) for t in token_reads]).astype(np.int64),
+        framed=np.frombuffer(b"".join(framed), dtype=np.uint8),
+        framed_offsets=np.cumsum([0] + [len(f) for f in framed]).astype(np.int64))
+    print("rna chunks", len(chunks), "tokens", len(tok), "words", sum(len(x) for x in streams) // 4)
+
+
 def _sharding_cases(path):
     """Read ranges of sample_balanced_ranges for edge cases and synthetic read sets."""
     sys.path.insert(0, str(path))
@@ -189,13 +223,15 @@ def _sharding_cases(path):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", "/root/reference"))
-    ap.add_argument("--only", choices=["sharding", "records"], default=None)
+    ap.add_argument("--only", choices=["sharding", "records", "rna"], default=None)
     args = ap.parse_args()
     os.environ.setdefault("NUMBA_CACHE_DIR", "/tmp/nbcache")
     if args.only in (None, "sharding"):
         _sharding_cases(Path(args.reference))
     if args.only in (None, "records"):
         _record_cases(Path(args.reference))
+    if args.only in (None, "rna"):
+        _rna_streams(Path(args.reference))
     if args.only is not None:
         return
     cc, ce, ci, sm = _import_reference(Path(args.reference))

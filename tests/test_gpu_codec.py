@@ -83,10 +83,11 @@ def test_mlp_logits_random_model_match_oracle(path, rows):
     assert (want == 127).any() or (want == -128).any() or rows < 128
 
 
-@pytest.mark.parametrize("name", ["lossless", "lossy"])
+@pytest.mark.parametrize("name", ["lossless", "lossy", "rna"])
 @pytest.mark.parametrize("path", ALL_PATHS)
 def test_streams_match_reference_golden(golden, name, path, request):
-    model = request.getfixturevalue(f"{name}_model")
+    # "rna": configuration-3-like reads coded with the lossless model
+    model = request.getfixturevalue(f"{'lossless' if name == 'rna' else name}_model")
     z = np.load(golden / f"streams_{name}.npz")
     chunks, ref = _chunks(z), _streams(z)
     codec = _codec(model, path)
@@ -95,9 +96,9 @@ def test_streams_match_reference_golden(golden, name, path, request):
     assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
 
 
-@pytest.mark.parametrize("name", ["lossless", "lossy"])
+@pytest.mark.parametrize("name", ["lossless", "lossy", "rna"])
 def test_read_framing_matches_reference_golden(golden, name, request):
-    model = request.getfixturevalue(f"{name}_model")
+    model = request.getfixturevalue(f"{'lossless' if name == 'rna' else name}_model")
     z = np.load(golden / f"streams_{name}.npz")
     reads = _chunks(z, "read_tokens", "read_offsets")
     framed_ref = [z["framed"][z["framed_offsets"][i]:z["framed_offsets"][i + 1]].tobytes()
