@@ -421,12 +421,13 @@ def main():
         def pinned(n, dt):
             return torch.empty(n, dtype=dt).pin_memory()
 
-        cap = pl.tok.numel()
+        # host buffers sized to this batch's record streams (the same every step), not to the
+        # device-side upper bounds: a rank pins about 2 x 2 B per sample plus the streams
         h_x = torch.from_numpy(samples_np).pin_memory()
         h_soff = torch.from_numpy(soff_np).pin_memory()
         h_y = pinned(n_samples, torch.int16)
-        h_words, h_woff = pinned(pl.words.numel(), torch.int32), pinned(pl.woff.numel(), torch.int64)
-        h_large, h_pos = pinned(cap, torch.int16), pinned(cap, torch.int32)
+        h_words, h_woff = pinned(n_words + 1, torch.int32), pinned(n_chunks + 1, torch.int64)
+        h_large, h_pos = pinned(max(n_large, 1), torch.int16), pinned(max(n_large, 1), torch.int32)
         h_sig0 = pinned(n_reads, torch.int16)
         h_tokoff, h_loff = pinned(n_reads + 1, torch.int64), pinned(n_reads + 1, torch.int64)
         moved = {"h2d": 0, "d2h": 0}
