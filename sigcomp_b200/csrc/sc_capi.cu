@@ -269,6 +269,10 @@ int sc_compress_chunks(sc_model *m, const uint8_t *tokens, const int64_t *token_
     }
     int rc = check_offsets(m, token_offsets, n_chunks);
     if (rc) return rc;
+    if (token_offsets[n_chunks] > 0 && !tokens) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
     cudaStream_t s = (cudaStream_t)stream;
     return guarded(m, [&]() -> int {
         const int64_t n_tok = token_offsets[n_chunks];
@@ -356,7 +360,7 @@ int sc_decompress_chunks(sc_model *m, const uint32_t *words, const int64_t *word
         }
         n_tok += lengths[c];
     }
-    if (n_tok > 0 && !tokens) {
+    if ((n_tok > 0 && !tokens) || (word_offsets[n_chunks] > 0 && !words)) {
         set_error("invalid argument");
         return SC_ERR_INVALID_ARGUMENT;
     }

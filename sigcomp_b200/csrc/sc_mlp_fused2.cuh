@@ -439,7 +439,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             bool dlive = false;
             DecState ds{};
             uint64_t dscale = 0, dq = 0;
-            if (DECODE && mine) {
+            if (DECODE && mine && L == NL - 1) {
                 drow = (int64_t)(2 * pt + (int)rank) * TM + r;
                 dlive = drow < p.n_rows;
                 dc = dlive ? p.order[drow] : 0;
@@ -469,11 +469,8 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             const int tile = 2 * pt + (int)rank;
             if (L < NL - 1) {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
-#pragma unroll 1
-                for (int c = part; c < TN / 32; c += EPI_PER_Q) {
-                    uint32_t va[32];
-                    tmem_ld32(taddr + c * 32, va);
-                    tmem_ld_wait();
+                // requantise chunk c (32 columns) of this row and store it to the activations
+                auto store_chunk = [&](const uint32_t (&va)[32], int c) {
                     const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
                     uint32_t packed[8];
                     if (rq_fast) {
@@ -486,10 +483,28 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
                     dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
                     dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                };
+                // chunks part, part + 3 and (parts 0 and 1) part + 6: each chunk's TMEM load is
+                // issued before the previous chunk is requantised, and the accumulator is
+                // released as soon as the last load has landed, before the last chunk's stores
+                const int c0 = part, c1 = part + EPI_PER_Q, c2 = part + 2 * EPI_PER_Q;
+                const bool three = c2 < TN / 32;                // warp-uniform
+                uint32_t va[32], vb[32];
+                tmem_ld32(taddr + c0 * 32, va);
+                tmem_ld_wait();
+                tmem_ld32(taddr + c1 * 32, vb);
+                store_chunk(va, c0);
+                tmem_ld_wait();
+                if (three) tmem_ld32(taddr + c2 * 32, va);
+                if (three) {
+                    store_chunk(vb, c1);
+                    tmem_ld_wait();
                 }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster_relaxed(acc_empty_leader);
+                if (three) store_chunk(va, c2);
+                else store_chunk(vb, c1);
                 if (nh == p.out_dim[L] / TN - 1) {
                     fence_proxy_async_global();
                     __syncwarp();

@@ -147,6 +147,49 @@ def test_corrupt_stream_raises(lossless_model):
     assert np.array_equal(codec.decompress_chunks([good], [50])[0], np.arange(50, dtype=np.uint8))
 
 
+
+def test_capi_rejects_bad_arguments(lossless_model):
+    """The host-buffer entry points validate sizes and pointers before any device work and
+    report SC_ERR_INVALID_ARGUMENT with a message; the handle stays usable."""
+    from sigcomp_b200 import _lib
+    codec = _codec(lossless_model)
+    lib, h = codec._lib, codec.handle
+    ptr = lambda a: ctypes.c_void_p(a.ctypes.data)
+    tok = np.arange(10, dtype=np.uint8)
+    words = np.zeros(64, np.uint32)
+    woff = np.zeros(3, np.int64)
+
+    def compress(tokens, off):
+        return lib.sc_compress_chunks(h, tokens, ptr(off), len(off) - 1, ptr(words), len(words), ptr(woff),
+                                      None, None)
+
+    cases = [
+        (None, np.asarray([0, 10], np.int64)),                       # tokens missing
+        (ptr(tok), np.asarray([1, 10], np.int64)),                   # offsets[0] != 0
+        (ptr(tok), np.asarray([0, 6, 4], np.int64)),                 # decreasing offsets
+    ]
+    for tokens, off in cases:
+        assert compress(tokens, off) == _lib.SC_ERR_INVALID_ARGUMENT
+        assert lib.sc_last_error()
+    long_tok = np.zeros(2049, np.uint8)
+    assert compress(ptr(long_tok), np.asarray([0, 2049], np.int64)) == _lib.SC_ERR_INVALID_ARGUMENT
+    assert b"chunk_len" in lib.sc_last_error()
+
+    out = np.zeros(16, np.uint8)
+
+    def decompress(w, off, lengths):
+        return lib.sc_decompress_chunks(h, w, ptr(off), ptr(lengths), len(lengths), ptr(out), None, None)
+
+    lens = np.asarray([10], np.int64)
+    assert decompress(None, np.asarray([0, 4], np.int64), lens) == _lib.SC_ERR_INVALID_ARGUMENT
+    assert decompress(ptr(words), np.asarray([1, 4], np.int64), lens) == _lib.SC_ERR_INVALID_ARGUMENT
+    assert decompress(ptr(words), np.asarray([0, 0], np.int64), lens) == _lib.SC_ERR_INVALID_ARGUMENT
+    assert decompress(ptr(words), np.asarray([0, 4], np.int64), np.asarray([2049], np.int64)) == \
+        _lib.SC_ERR_INVALID_ARGUMENT
+    # still usable
+    streams = codec.compress_chunks([tok])
+    assert np.array_equal(codec.decompress_chunks(streams, [10])[0], tok)
+
 def test_truncated_and_mismatched_streams_match_oracle(lossless_model):
     codec = _codec(lossless_model)
     om = OracleModel(lossless_model)
