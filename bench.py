@@ -48,6 +48,7 @@ sys.path.insert(0, str(REPO))
 METRIC = "compress & decompress Msamples/s at 1/2/4/8 B200; bits/sample (bit-exact)"
 UNIT = "Msamples/s"
 CHUNK_LEN = 2048
+L2_BYTES = 126 * 1024 * 1024           # B200 L2
 # int8 MLP work per coded token: 2 x (8192*512 + 7*512*512 + 512*256) multiply-adds
 OPS_PER_TOKEN = 2 * (8192 * 512 + 7 * 512 * 512 + 512 * 256)
 # BASELINE.json configurations: (generator, reads, model, lossy lsb, description).  Configuration 2 is
@@ -529,7 +530,11 @@ def main():
                        "reads_per_gpu": args.reads, "samples_per_gpu": n_samples, "tokens_per_gpu": n_tok,
                        "chunks_per_gpu": n_chunks, "parallelism": f"reads sharded over {world} GPU(s)",
                        "step": "split -> compress -> decompress -> reassemble, int16 reads in and out",
-                       "l2": "inputs larger than L2 (1.6 GB of samples per GPU); no flush needed"},
+                       "l2": (f"inputs larger than L2 ({2 * n_samples / 1e9:.2f} GB of samples, "
+                              f"{n_tok / 1e9:.2f} GB of tokens per GPU); no flush needed"
+                              if 2 * n_samples > L2_BYTES else
+                              f"inputs ({2 * n_samples / 1e6:.1f} MB of samples per GPU) fit in L2 and are "
+                              "not flushed between steps")},
             "compress_msps": round(total_samples * args.steps / (t_comp_max * 1e-3) / 1e6, 3),
             "decompress_msps": round(total_samples * args.steps / (t_dec_max * 1e-3) / 1e6, 3),
             "bits_per_sample_neural": round(8 * total_stream / total_samples, 4),
