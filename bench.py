@@ -120,6 +120,14 @@ def chunk_offsets(tok_off, chunk_len):
     return np.append(starts, tok_off[-1]).astype(np.int64)
 
 
+def smi_gpu_id(local, env=None):
+    """The nvidia-smi --id of CUDA device `local`: nvidia-smi numbers GPUs physically, so a
+    CUDA_VISIBLE_DEVICES list (indices or UUIDs, both accepted by --id) maps the ordinal."""
+    env = os.environ if env is None else env
+    vis = [v.strip() for v in env.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    return vis[local] if local < len(vis) else str(local)
+
+
 class ClockSampler:
     """nvidia-smi clock / throttle sampling during the timed region."""
 
@@ -134,7 +142,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={smi_gpu_id(self.index)}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None

@@ -42,3 +42,11 @@ def test_lossy_round_trip_matches_signal_module():
     y = bench.lossy_round_trip(x, 3)
     assert np.array_equal(y, signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(x, 3), 3), 3))
     assert np.all(np.abs(y.astype(np.int32) - x.astype(np.int32))[:6] <= 4)
+
+
+def test_clock_sampler_maps_visible_devices():
+    assert bench.smi_gpu_id(0, {}) == "0"
+    assert bench.smi_gpu_id(3, {}) == "3"
+    assert bench.smi_gpu_id(0, {"CUDA_VISIBLE_DEVICES": "4,5"}) == "4"
+    assert bench.smi_gpu_id(1, {"CUDA_VISIBLE_DEVICES": " 4, 5 "}) == "5"
+    assert bench.smi_gpu_id(0, {"CUDA_VISIBLE_DEVICES": "GPU-1234abcd"}) == "GPU-1234abcd"
