@@ -126,6 +126,21 @@ def test_edge_chunks(lossless_model):
     assert codec.decompress_chunks([], []) == []
 
 
+
+@pytest.mark.parametrize("chunk_len", [1, 63, 64, 65, 129, 300, 4096, 65535])
+def test_chunk_lengths_match_oracle(lossless_model, chunk_len):
+    """chunk_len is a codec parameter (1..65535, the '<H' frame): windows shorter than 64, tiles
+    of 128 rows cut at chunk ends and the longest decoder launches all stay bit-exact, with full,
+    short and empty chunks in one batch."""
+    codec = _codec(lossless_model, chunk_len=chunk_len)
+    rng = np.random.default_rng(chunk_len)
+    chunks = [rng.integers(0, 40, size=chunk_len).astype(np.uint8) for _ in range(1 if chunk_len > 5000 else 3)]
+    chunks += [rng.integers(0, 256, size=max(chunk_len // 3, 1)).astype(np.uint8), np.empty(0, np.uint8)]
+    streams = codec.compress_chunks(chunks)
+    assert streams == OracleModel(lossless_model).compress_chunks(chunks, chunk_len=chunk_len)
+    back = codec.decompress_chunks(streams, [len(c) for c in chunks])
+    assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
+
 def test_reads_without_small_tokens(lossless_model):
     codec = _codec(lossless_model)
     reads = [np.empty(0, np.uint8), np.asarray([7, 9], np.uint8), np.empty(0, np.uint8)]
