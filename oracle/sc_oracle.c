@@ -283,10 +283,31 @@ int sco_mlp_rows(const sco_model *m, const int16_t *windows, int64_t rows, int8_
     return 0;
 }
 
-/* Linear epilogue on a precomputed int32 accumulator (for the int_mm baseline). */
+/* Linear epilogue on a precomputed int32 accumulator (for the int_mm baseline).
+ * With m0 < 2^31 and shift >= 32 (the exported models' case) the product's floor
+ * division runs on 32-bit lanes: floor(p / 2^s) = floor(floor(p / 2^32) / 2^(s-32)),
+ * and floor(p / 2^32) is the high word of the 64-bit product; otherwise every
+ * element takes sco_requantize.  Both give sco_requantize's value. */
 void sco_epilogue(const int32_t *acc, int64_t rows, int32_t n, const int32_t *bias,
                   int64_t m0, int32_t shift, int32_t relu, int8_t *out)
 {
+    if (m0 >= 0 && m0 < ((int64_t)1 << 31) && shift >= 32 && shift <= 63) {
+        const int32_t m = (int32_t)m0, sh = shift - 32, lo = relu ? 0 : -128;
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; ++r) {
+            const int32_t *a = acc + r * n;
+            int8_t *o = out + r * n;
+            for (int32_t c = 0; c < n; ++c) {
+                const int32_t b = (int32_t)((uint32_t)a[c] + (uint32_t)bias[c]);   /* int32 wrap */
+                const int32_t hi = (int32_t)(((int64_t)b * m) >> 32);
+                int32_t v = hi >> sh;
+                v = v < lo ? lo : v;
+                v = v > 127 ? 127 : v;
+                o[c] = (int8_t)v;
+            }
+        }
+        return;
+    }
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; ++r)
         for (int32_t c = 0; c < n; ++c)
@@ -460,7 +481,10 @@ int sco_gather_windows(const sco_model *m, const int16_t *windows, int64_t rows,
         for (int p = 0; p < W; ++p) {
             const int tok = windows[r * W + p];
             if (tok < 0 || tok > SCO_SOS) { bad = 1; continue; }
-            memcpy(x + (r * W + p) * E, m->embedding + (size_t)tok * E, (size_t)E);
+            if (E == 128)          /* the exported models' width: a fixed-size copy */
+                memcpy(x + (r * W + p) * 128, m->embedding + (size_t)tok * 128, 128);
+            else
+                memcpy(x + (r * W + p) * E, m->embedding + (size_t)tok * E, (size_t)E);
         }
     }
     return bad;
