@@ -78,7 +78,9 @@ def parse_args():
                     help="BASELINE configuration (config2, the headline, by default)")
     ap.add_argument("--reads", type=int, default=None,
                     help="reads per GPU per step (default: the configuration's read count)")
-    ap.add_argument("--cpu-reads", type=int, default=12, help="reads in the CPU baseline sample")
+    ap.add_argument("--cpu-reads", type=int, default=32,
+                    help="reads in the CPU baseline sample (about 1.6 M samples: 10-20 s of CPU work per "
+                         "warm-up + round trip)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
