@@ -122,9 +122,20 @@ def chunk_offsets(tok_off, chunk_len):
     return np.append(starts, tok_off[-1]).astype(np.int64)
 
 
-def smi_gpu_id(local, env=None):
-    """The nvidia-smi --id of CUDA device `local`: nvidia-smi numbers GPUs physically, so a
+def smi_gpu_id(local, env=None, props=None):
+    """The nvidia-smi --id of CUDA device `local`.  CUDA ordinals and nvidia-smi indices can
+    differ (CUDA_VISIBLE_DEVICES, device order), so the GPU is named by its PCI address
+    (domain:bus:device.function, as nvidia-smi prints it); without device properties, a
     CUDA_VISIBLE_DEVICES list (indices or UUIDs, both accepted by --id) maps the ordinal."""
+    if props is None:
+        try:
+            import torch
+            if torch.cuda.is_available():
+                props = torch.cuda.get_device_properties(local)
+        except Exception:
+            props = None
+    if props is not None:
+        return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
     env = os.environ if env is None else env
     vis = [v.strip() for v in env.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
     return vis[local] if local < len(vis) else str(local)

@@ -44,7 +44,15 @@ def test_lossy_round_trip_matches_signal_module():
     assert np.all(np.abs(y.astype(np.int32) - x.astype(np.int32))[:6] <= 4)
 
 
-def test_clock_sampler_maps_visible_devices():
+def test_clock_sampler_names_the_gpu_by_pci_address():
+    class Props:
+        pci_domain_id, pci_bus_id, pci_device_id = 0, 0x1B, 0
+    assert bench.smi_gpu_id(3, {"CUDA_VISIBLE_DEVICES": "5"}, Props()) == "00000000:1B:00.0"
+
+
+def test_clock_sampler_maps_visible_devices(monkeypatch):
+    import torch
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: False)      # no device properties
     assert bench.smi_gpu_id(0, {}) == "0"
     assert bench.smi_gpu_id(3, {}) == "3"
     assert bench.smi_gpu_id(0, {"CUDA_VISIBLE_DEVICES": "4,5"}) == "4"
