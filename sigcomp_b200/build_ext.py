@@ -17,6 +17,30 @@ FLAGS = [
 ]
 
 
+# Kernels whose tcgen05.ld results land in registers asynchronously (until tcgen05.wait::ld):
+# a register spill placed between a load and its wait would store values not yet written, so the
+# build refuses any spill in them.  ptxas -v reports stack and spills per entry function.
+NO_SPILL_KERNELS = ("k_fused2",)
+NO_SPILL_SOURCE = "sc_mlp_tc.cu"
+
+
+def spilling_kernels(ptxas_log, names=NO_SPILL_KERNELS):
+    """[(mangled name, spill store bytes, spill load bytes)] of the entry functions in a
+    `ptxas -v` log whose name contains one of `names` and that spill."""
+    bad, current = [], None
+    for line in ptxas_log.splitlines():
+        if "Function properties for" in line:
+            current = line.split("Function properties for", 1)[1].strip()
+        elif current is not None and "spill stores" in line:
+            parts = line.replace(",", "").split()
+            stores = int(parts[parts.index("spill") - 2])
+            loads = int(parts[parts.index("loads") - 3])
+            if any(n in current for n in names) and (stores or loads):
+                bad.append((current, stores, loads))
+            current = None
+    return bad
+
+
 def _stale():
     if not LIB.exists():
         return True
@@ -35,7 +59,8 @@ def build(force=False, verbose=False, jobs=4):
     procs = []
     for src in SOURCES:
         obj = build_dir / (src + ".o")
-        cmd = [NVCC, *FLAGS, "-dc" if False else "-c", str(CSRC / src), "-o", str(obj)]
+        extra = ["-Xptxas", "-v"] if src == NO_SPILL_SOURCE else []
+        cmd = [NVCC, *FLAGS, *extra, "-c", str(CSRC / src), "-o", str(obj)]
         if verbose:
             print(" ".join(cmd))
         procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT)))
@@ -45,7 +70,14 @@ def build(force=False, verbose=False, jobs=4):
         out, _ = p.communicate()
         if p.returncode != 0:
             failed.append((src, out.decode()))
-        elif verbose and out:
+            continue
+        if src == NO_SPILL_SOURCE:
+            spills = spilling_kernels(out.decode())
+            if spills:
+                failed.append((src, "register spills in kernels that must not spill: " + "; ".join(
+                    f"{name}: {st} B stored, {ld} B loaded" for name, st, ld in spills)))
+                continue
+        if verbose and out:
             print(out.decode())
     if failed:
         for src, out in failed:

@@ -171,3 +171,20 @@ def test_read_framing_matches_reference_golden_on_cpu(golden, name, request):
     assert codec.batch_inference_reads(list_of_reads=reads) == framed_ref
     back = codec.batch_inference_reads(list_of_compressed_reads=framed_ref, list_of_lengths=[len(r) for r in reads])
     assert all(np.array_equal(a, b) for a, b in zip(back, reads))
+
+
+def test_build_refuses_spills_in_the_fused_kernels():
+    """The build fails if ptxas spills registers in a kernel whose tcgen05.ld results are in flight
+    in registers; other kernels may spill."""
+    from sigcomp_b200.build_ext import spilling_kernels
+    log = "\n".join([
+        "ptxas info    : Function properties for _ZN2sc12_GLOBAL__N_18k_fused2ILb1EEEvNS_12Fused2ParamsE",
+        "    48 bytes stack frame, 36 bytes spill stores, 44 bytes spill loads",
+        "ptxas info    : Used 128 registers, used 1 barriers, 48 bytes cumulative stack size",
+        "ptxas info    : Function properties for _ZN2sc12_GLOBAL__N_18k_fused2ILb0EEEvNS_12Fused2ParamsE",
+        "    0 bytes stack frame, 0 bytes spill stores, 0 bytes spill loads",
+        "ptxas info    : Function properties for _ZN2sc7k_layerEv",
+        "    0 bytes stack frame, 8 bytes spill stores, 8 bytes spill loads",
+    ])
+    assert spilling_kernels(log) == [("_ZN2sc12_GLOBAL__N_18k_fused2ILb1EEEvNS_12Fused2ParamsE", 36, 44)]
+    assert spilling_kernels(log.replace("36 bytes spill stores, 44", "0 bytes spill stores, 0")) == []
