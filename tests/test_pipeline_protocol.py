@@ -75,14 +75,25 @@ def units(decode, n_tiles, maxlen):
                         yield grp, tt, g0 + tt, step, L, nh
 
 
-def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None):
+def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slots=False):
     """Run one pair's roles to completion.  `plant` injects one protocol mistake into the model
     (tests of the model itself): 'counter' (a producer waits for one layer less), 'warp' (one
-    epilogue warp missing) or 'stages' (the MMA cycles over one stage less than the producer)."""
+    epilogue warp missing) or 'stages' (the MMA cycles over one stage less than the producer).
+    With `slots`, the operand buffers are a ring of 16 KB slots with a barrier pair per slot: a
+    dual layer-0 K block takes three slots, every other K block two (12 slots for the decoder's
+    192 KB, 8 for compression's 128 KB); each role tracks a slot's phase per slot."""
     rng = random.Random(seed)
     in_dim = [l0_kblocks * KB] + [512] * (NL - 1)
-    full = [Bar(f"full{s}", 1) for s in range(STAGES)]
-    empty = [[Bar(f"empty{s}/cta{r}", 1) for s in range(STAGES)] for r in range(2)]
+    nbuf = (12 if decode else 8) if slots else STAGES
+    full = [Bar(f"full{s}", 1) for s in range(nbuf)]
+    empty = [[Bar(f"empty{s}/cta{r}", 1) for s in range(nbuf)] for r in range(2)]
+
+    def kblock_bufs(L, pos, it, n_ring):
+        """The buffers (stage, or slots) of a K block and how far the position advances."""
+        if not slots:
+            return [it % n_ring], 1
+        n = 3 if (decode and L == 0) else 2
+        return [(pos + i) % n_ring for i in range(n)], n
     acc_full = [[Bar(f"acc_full{b}/cta{r}", 1) for b in range(2)] for r in range(2)]
     acc_empty = [Bar(f"acc_empty{b}", 2 * EPI_WARPS) for b in range(2)]
     g_full = [Bar(f"g_full{b}", 4) for b in range(2)]
@@ -96,7 +107,8 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None):
             yield
 
     def producer(rank):
-        it = 0
+        it = pos = 0
+        uses = [0] * nbuf                             # per buffer: times filled so far
         for grp, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
             if decode and L == 0 and nh == 1:
                 continue                              # loaded with half 0
@@ -113,8 +125,12 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None):
 
             kstep = 2 if (not decode and L == 0) else 1
             for kb in range(0, nkb, kstep):
-                s = it % STAGES
-                yield from parity_wait(empty[rank][s], ((it // STAGES) & 1) ^ 1, it // STAGES)
+                bufs, adv = kblock_bufs(L, pos, it, nbuf)
+                for j in bufs:
+                    u = uses[j]
+                    yield from parity_wait(empty[rank][j], (u & 1) ^ 1, u)
+                    uses[j] += 1
+                s = bufs[0]
                 dual = decode and L == 0
                 a_tma = decode or L != 0
                 nbytes = 2 * ((2 if dual else 1) * 16 + (16 if a_tma else 16))
@@ -123,10 +139,12 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None):
                     full[s].arrive()
                 tma.append((full[s], nbytes // 2))    # this CTA's share completes on the leader
                 it += 1
+                pos += adv
                 yield
 
     def mma():
-        it = uu = li = 0
+        it = uu = li = pos = 0
+        firsts = [0] * nbuf                           # per buffer: K blocks it has led so far
         for grp, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
             if decode and L == 0 and nh == 1:
                 continue
@@ -141,10 +159,15 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None):
                 yield from parity_wait(g_full[gb], (li >> 1) & 1, (li >> 1) + 1)
             kstep = 2 if (not decode and L == 0) else 1
             for kb in range(0, nkb, kstep):
-                s = it % (STAGES - 1 if plant == "stages" else STAGES)
-                yield from parity_wait(full[s], (it // STAGES) & 1, it // STAGES + 1)
-                commits.append([empty[0][s], empty[1][s]])
+                bufs, adv = kblock_bufs(L, pos, it, nbuf - 1 if plant == "stages" else nbuf)
+                s = bufs[0]
+                f = firsts[s]
+                yield from parity_wait(full[s], f & 1, f + 1)
+                firsts[s] += 1
+                for j in bufs:                        # one commit per buffer, in order
+                    commits.append([empty[0][j], empty[1][j]])
                 it += 1
+                pos += adv
                 yield
             commits.append([acc_full[0][ab], acc_full[1][ab]])
             if dual:
@@ -221,16 +244,25 @@ def test_compress_protocol(n_tiles, seed):
     simulate(False, n_tiles, seed=seed)
 
 
+@pytest.mark.parametrize("seed", range(3))
+@pytest.mark.parametrize("decode,n_tiles,maxlen", [(True, 4, [3, 3, 2, 1]), (True, 12, [2] * 12),
+                                                  (True, 11, [3, 3, 3, 2, 2, 2, 2, 1, 1, 1, 1]), (False, 23, None)])
+def test_slot_ring_protocol(decode, n_tiles, maxlen, seed):
+    """The 16 KB slot ring (a deeper prefetch for hidden layers) keeps every invariant."""
+    simulate(decode, n_tiles, maxlen, seed=seed, slots=True)
+
+
+@pytest.mark.parametrize("slots", [False, True])
 @pytest.mark.parametrize("plant,messages", [("counter", ("loaded before it was written",)),
                                             ("warp", ("deadlock",)),
                                             ("stages", ("waiter targets phase", "deadlock"))])
-def test_the_model_catches_planted_protocol_mistakes(plant, messages):
+def test_the_model_catches_planted_protocol_mistakes(plant, messages, slots):
     """Each planted mistake fails the model under some interleaving, for the expected reason."""
     errors = []
     for seed in range(4):
         for decode, n_tiles, maxlen in [(True, 4, [3, 3, 2, 1]), (True, 12, [2] * 12), (False, 10, None)]:
             try:
-                simulate(decode, n_tiles, maxlen, seed=seed, plant=plant)
+                simulate(decode, n_tiles, maxlen, seed=seed, plant=plant, slots=slots)
             except AssertionError as e:
                 errors.append(str(e))
     assert errors and all(any(m in e for m in messages) for e in errors), errors[:3]
