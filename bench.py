@@ -95,11 +95,15 @@ def parse_args():
 
 
 def lossy_round_trip(x, lsb):
-    """What SigComp's lossy mode returns for samples x (main.py:158-171, 1162-1164)."""
-    from sigcomp_b200 import signal
+    """What SigComp's lossy mode returns for int16 samples x: _lossy_decode(_lossy_encode(
+    _reduce_lsb(x, lsb), lsb), lsb) (main.py:158-171, 1162-1164).  _reduce_lsb rounds x to a
+    multiple of 2**lsb in int32 and wraps it to int16; the shift down and back up then returns
+    that value unchanged."""
     if lsb == 0:
         return x
-    return signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(x, lsb), lsb), lsb)
+    v = np.asarray(x).astype(np.int32)
+    step = 1 << lsb
+    return ((v & ~(step - 1)) + ((v >> (lsb - 1)) & 1) * step).astype(np.int16)
 
 
 def make_reads(rank, n_reads, generator="r10_lognormal"):
@@ -213,8 +217,8 @@ def cpu_round_trip(reads, chunk_len, steps=1, warmup=1, lsb=0, model="lossless")
     """The reference path ported to the CPU: numpy split / reassembly (sigcomp_b200.signal,
     pinned to the reference's outputs) around the oracle codec (int_mm GEMMs + C coder)."""
     import torch
+    from oracle import signal
     from oracle.oracle import OracleModel
-    from sigcomp_b200 import signal
     from sigcomp_b200.model import load_model
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)

@@ -1,8 +1,10 @@
-"""Host-side signal transform on either side of the neural codec.
+"""Host restatement of SigComp's signal transform on either side of the neural codec.
 
-These functions restate SigComp's delta / zig-zag / split step so that the
-benchmark and the tests can turn int16 reads into the uint8 token streams the
-codec consumes, and back.  They follow ``sigcomp/main.py``:
+Test infrastructure, like the rest of ``oracle/``: the tests, ``smoke()`` and the
+CPU-baseline leg of ``bench.py`` use it as the checker of the GPU signal kernels
+(``sc_split_signal_device`` / ``sc_reassemble_signal_device``) and to turn int16
+reads into token streams on the CPU.  The product package never imports it.
+The functions follow ``sigcomp/main.py``:
 
 * ``delta_zigzag_encode``  - ``_diff_encode`` + ``_zigzag_encode`` (main.py:129-155)
 * ``reduce_lsb`` / ``lossy_encode`` / ``lossy_decode`` - main.py:158-171

@@ -41,11 +41,15 @@ int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *of
 
 namespace {
 
+// Makes the model's device current for one call and restores the caller's device after it.
+// `err` records a failed switch; guarded() turns it into an error before any launch, so a call
+// never runs on another device with this model's pointers.
 struct DeviceGuard {
     int prev = -1;
+    cudaError_t err = cudaSuccess;
     explicit DeviceGuard(int dev) {
         cudaGetDevice(&prev);
-        if (prev != dev) cudaSetDevice(dev);
+        if (prev != dev) err = cudaSetDevice(dev);
     }
     ~DeviceGuard() {
         if (prev >= 0) cudaSetDevice(prev);
@@ -63,6 +67,7 @@ int guarded(sc_model *m, F &&f)
 {
     try {
         DeviceGuard g(m->device);
+        SC_CUDA(g.err);
         int rc = f();
         if (m->prof.on) {
             SC_CUDA(cudaDeviceSynchronize());
@@ -78,6 +83,9 @@ int guarded(sc_model *m, F &&f)
     } catch (const std::bad_alloc &) {
         set_error("host out of memory");
         return SC_ERR_OUT_OF_MEMORY;
+    } catch (...) {
+        set_error("internal error");
+        return SC_ERR_CUDA;
     }
 }
 
@@ -98,6 +106,22 @@ int check_offsets(const sc_model *m, const int64_t *off, int64_t n)
             set_error("A token chunk exceeds chunk_len");
             return SC_ERR_INVALID_ARGUMENT;
         }
+    }
+    return SC_OK;
+}
+
+// Automatic selection (path 0) runs only the tcgen05 kernels: the fused pair kernels for
+// compress/decompress and the tcgen05 layer kernels for the logits entry point.  A model
+// whose geometry they do not cover is refused with SC_ERR_UNSUPPORTED instead of being run
+// on another implementation; the other implementations run only when a caller selects them
+// with sc_model_set_mlp_path (cross-checks in the tests).
+int check_auto_path(const sc_model *m, bool fused)
+{
+    if (m->mlp_path != 0) return SC_OK;
+    if (!m->tc_ok || (fused && !fused_supported(m))) {
+        set_error("model geometry not supported by the tcgen05 kernels (window 64, emb_dim 128, layer widths "
+                  "multiples of 256 up to 512, at most 9 layers)");
+        return SC_ERR_UNSUPPORTED;
     }
     return SC_OK;
 }
@@ -269,6 +293,7 @@ int sc_compress_chunks(sc_model *m, const uint8_t *tokens, const int64_t *token_
     }
     int rc = check_offsets(m, token_offsets, n_chunks);
     if (rc) return rc;
+    if ((rc = check_auto_path(m, true))) return rc;
     if (token_offsets[n_chunks] > 0 && !tokens) {
         set_error("invalid argument");
         return SC_ERR_INVALID_ARGUMENT;
@@ -311,6 +336,7 @@ int sc_compress_chunks_device(sc_model *m, const uint8_t *tokens, const int64_t 
         set_error("invalid argument");
         return SC_ERR_INVALID_ARGUMENT;
     }
+    if (int rc = check_auto_path(m, true)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     return guarded(m, [&]() -> int {
         std::vector<int64_t> off_h(n_chunks + 1);
@@ -364,6 +390,7 @@ int sc_decompress_chunks(sc_model *m, const uint32_t *words, const int64_t *word
         set_error("invalid argument");
         return SC_ERR_INVALID_ARGUMENT;
     }
+    if (int rc = check_auto_path(m, true)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     return guarded(m, [&]() -> int {
         const int64_t n_words = word_offsets[n_chunks];
@@ -406,6 +433,7 @@ int sc_decompress_chunks_device(sc_model *m, const uint32_t *words, const int64_
             set_error("Chunk lengths must be integers in [0, chunk_len]");
             return SC_ERR_INVALID_ARGUMENT;
         }
+    if (int rc = check_auto_path(m, true)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     return guarded(m, [&]() -> int {
         uint8_t *d_err = chunk_errors ? chunk_errors : (uint8_t *)m->ws_err.get((size_t)n_chunks + 16, s);
@@ -579,6 +607,7 @@ int sc_mlp_logits_device(sc_model *m, const int16_t *windows, int64_t rows, int8
         set_error("invalid argument");
         return SC_ERR_INVALID_ARGUMENT;
     }
+    if (int rc = check_auto_path(m, false)) return rc;
     cudaStream_t s = (cudaStream_t)stream;
     return guarded(m, [&]() -> int {
         run_mlp(m, windows, rows, logits, s);

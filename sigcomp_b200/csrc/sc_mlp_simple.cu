@@ -183,7 +183,15 @@ extern "C" SC_API int sc_mlp_logits_device_noalloc(sc_model *m, const int16_t *w
     cudaStream_t s = (cudaStream_t)stream;
     int prev = -1;
     cudaGetDevice(&prev);
-    if (prev != m->device) cudaSetDevice(m->device);
+    if (prev != m->device) {
+        // the scratch address and the weights belong to the model's device: never launch elsewhere
+        const cudaError_t e = cudaSetDevice(m->device);
+        if (e != cudaSuccess) {
+            set_error("CUDA error %s (%s) selecting device %d", cudaGetErrorName(e), cudaGetErrorString(e),
+                      m->device);
+            return SC_ERR_CUDA;
+        }
+    }
     int rc = SC_OK;
     try {
         if (rows > 0) {
@@ -209,6 +217,10 @@ extern "C" SC_API int sc_mlp_logits_device_noalloc(sc_model *m, const int16_t *w
     } catch (const CudaError &e) {
         set_error("CUDA error %s (%s) in %s", cudaGetErrorName(e.code), cudaGetErrorString(e.code),
                   e.where.c_str());
+        rc = SC_ERR_CUDA;
+    } catch (...) {
+        // nothing may cross the C boundary (the scratch lookup takes a lock, which can throw)
+        set_error("sc_mlp_logits_device_noalloc: internal error");
         rc = SC_ERR_CUDA;
     }
     if (prev >= 0 && prev != m->device) cudaSetDevice(prev);

@@ -24,7 +24,6 @@ import numpy as np
 
 from .codec import B200Compression
 from .model import load_model
-from .signal import split_signal
 from .synthetic import make_reads
 
 ROLES = {0: "producer", 1: "mma", 2: "epilogue", 3: "builder"}
@@ -93,14 +92,14 @@ def main(argv=None):
     model = load_model(name="lossless")
     reads = make_reads("r10_lognormal", seed=5, count=args.reads)
     L = args.chunk_len
+    codec = B200Compression(chunk_len=L, gpu=args.gpu, model=model)
     chunks = []
-    for r in reads:
-        tok = split_signal(r)[1]
+    for sp in codec.split_signals(reads):            # _split_signal on the GPU
+        tok = sp[1]
         chunks += [tok[i:i + L] for i in range(0, len(tok), L)]
     off = np.zeros(len(chunks) + 1, np.int64)
     off[1:] = np.cumsum([len(c) for c in chunks])
     tokens = np.concatenate(chunks)
-    codec = B200Compression(chunk_len=L, gpu=args.gpu, model=model)
     lib = codec._lib
     buf = np.zeros((args.records, 2), np.uint64)
 

@@ -222,7 +222,9 @@ def _sharding_cases(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", str(REPO / "baseline" / "_ref")),
+                    help="root of the SigComp source tree (holding sigcomp/); default: $SIGCOMP_REFERENCE, "
+                         "else the offline install under baseline/_ref")
     ap.add_argument("--only", choices=["sharding", "records", "rna"], default=None)
     args = ap.parse_args()
     os.environ.setdefault("NUMBA_CACHE_DIR", "/tmp/nbcache")

@@ -36,12 +36,16 @@ def test_workloads_cover_baseline_configurations():
 
 
 def test_lossy_round_trip_matches_signal_module():
-    from sigcomp_b200 import signal
+    from oracle import signal
     x = np.asarray([0, 1, 7, 8, 9, -5, 32767, -32768, 1234], dtype=np.int16)
     assert np.array_equal(bench.lossy_round_trip(x, 0), x)
     y = bench.lossy_round_trip(x, 3)
     assert np.array_equal(y, signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(x, 3), 3), 3))
     assert np.all(np.abs(y.astype(np.int32) - x.astype(np.int32))[:6] <= 4)
+    z = np.random.default_rng(9).integers(-32768, 32768, size=20000).astype(np.int16)
+    for lsb in range(1, 9):
+        assert np.array_equal(bench.lossy_round_trip(z, lsb),
+                              signal.lossy_decode(signal.lossy_encode(signal.reduce_lsb(z, lsb), lsb), lsb))
 
 
 def test_clock_sampler_names_the_gpu_by_pci_address():

@@ -239,7 +239,8 @@ def test_random_model_streams_match_oracle(path):
 
 
 def test_synthetic_reads_match_oracle(lossless_model):
-    from sigcomp_b200 import signal, synthetic
+    from oracle import signal
+    from sigcomp_b200 import synthetic
     reads = synthetic.make_reads("r10_config1", seed=1, count=2)
     toks = [signal.split_signal(r)[1] for r in reads]
     chunks = []
@@ -253,7 +254,8 @@ def test_synthetic_reads_match_oracle(lossless_model):
 def test_large_round_trip_properties(lossless_model):
     """Config-2-shaped reads at a size the oracle cannot check directly: round trip
     identity, determinism, and agreement of the two MLP paths."""
-    from sigcomp_b200 import signal, synthetic
+    from oracle import signal
+    from sigcomp_b200 import synthetic
     reads = synthetic.make_reads("r10_lognormal", seed=2, count=60)
     toks = [signal.split_signal(r)[1] for r in reads]
     codec = _codec(lossless_model)

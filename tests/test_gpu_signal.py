@@ -6,7 +6,8 @@ against the host restatement of SigComp's _split_signal / _reassemble_signal
 import numpy as np
 import pytest
 
-from sigcomp_b200 import signal, synthetic
+from oracle import signal
+from sigcomp_b200 import synthetic
 
 pytestmark = pytest.mark.gpu
 

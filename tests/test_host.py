@@ -7,7 +7,8 @@ import ctypes
 import numpy as np
 import pytest
 
-from sigcomp_b200 import _lib, signal, synthetic
+from oracle import signal
+from sigcomp_b200 import _lib, synthetic
 from conftest import REPO
 
 

@@ -8,7 +8,7 @@ from hypothesis import strategies as st
 from hypothesis.extra import numpy as hnp
 
 import bench
-from sigcomp_b200 import signal
+from oracle import signal
 from sigcomp_b200.records import REC_FMT, pack_records, parse_records
 
 int16_reads = hnp.arrays(np.int16, st.integers(1, 400),
