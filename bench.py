@@ -81,6 +81,9 @@ def parse_args():
     ap.add_argument("--cpu-reads", type=int, default=32,
                     help="reads in the CPU baseline sample (about 1.6 M samples: 10-20 s of CPU work per "
                          "warm-up + round trip)")
+    ap.add_argument("--parity-reads", type=int, default=200,
+                    help="reads whose GPU streams the CPU-baseline leg compares with the oracle's (compress "
+                         "only, int_mm MLP: a few seconds of CPU work per 100 reads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
@@ -249,6 +252,35 @@ def cpu_round_trip(reads, chunk_len, steps=1, warmup=1, lsb=0, model="lossless")
     td = sum(t[1] for t in times) / len(times)
     return {"value": samples / (tc + td) / 1e6, "compress": samples / tc / 1e6, "decompress": samples / td / 1e6,
             "cores": cores, "seconds_per_step": tc + td, "samples": samples}
+
+
+def parity_vs_oracle(pl, reads, n_reads, chunk_len, lsb, model):
+    """Compare the GPU streams of the first `n_reads` reads of the batch (the chunks the last
+    timed compress wrote) with the oracle's streams for the same reads: the oracle's split
+    (main.py:504-521) and its compress_chunks with the int_mm MLP (cpu_compression.py:178-257),
+    both pinned to the reference's outputs by the golden tests."""
+    from oracle import signal
+    from oracle.oracle import OracleModel
+    from sigcomp_b200.model import load_model
+    n = min(n_reads, len(reads))
+    tok_off = pl.tok_off[:n + 1].cpu().numpy()
+    ntok = np.diff(tok_off)
+    k = int(((ntok + chunk_len - 1) // chunk_len).sum())
+    woff = pl.woff[:k + 1].cpu().numpy()
+    words = pl.words[:int(woff[k])].cpu().numpy().view(np.uint32)
+    gpu = [words[woff[i]:woff[i + 1]].astype("<u4").tobytes() for i in range(k)]
+    splits = signal.reads_to_tokens(reads[:n], lsb)
+    chunks = [sp[1][j:j + chunk_len] for sp in splits for j in range(0, len(sp[1]), chunk_len)]
+    t0 = time.perf_counter()
+    ref = OracleModel(load_model(name=model)).compress_chunks(chunks, chunk_len=chunk_len, backend="int_mm")
+    dt = time.perf_counter() - t0
+    mismatch = next((i for i, (a, b) in enumerate(zip(gpu, ref)) if a != b), None)
+    equal = len(chunks) == k and mismatch is None
+    return {"reads": n, "chunks": k, "tokens": int(ntok.sum()), "equal": bool(equal),
+            "first_mismatch": mismatch, "oracle_seconds": round(dt, 2),
+            "what": "GPU chunk streams of the timed batch's first reads vs the CPU oracle's (oracle/: C coder "
+                    "+ int_mm MLP, pinned to the reference's golden streams); decoded reads are checked "
+                    "separately against the input (bit_exact_round_trip)"}
 
 
 def run_reference(args):
@@ -536,8 +568,10 @@ def main():
             roofline["kernel_ms"] = {k: round(v[0], 2) for k, v in prof.items()}
             roofline["kernel_launches"] = {k: v[1] for k, v in prof.items()}
 
-    cpu = None
+    cpu = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if args.parity_reads > 0:
+            parity = parity_vs_oracle(pl, reads, args.parity_reads, args.chunk_len, args.lsb, args.model)
         n = min(args.cpu_reads, args.reads)
         r = cpu_round_trip(reads[:n], args.chunk_len, steps=1, warmup=1, lsb=args.lsb, model=args.model)
         cpu = {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
@@ -566,6 +600,7 @@ def main():
             "bits_per_small_token": round(8 * total_stream / total_tokens, 4),
             "large_delta_fraction": round(total_large / max(total_samples, 1), 5),
             "bit_exact_round_trip": all_ok,
+            "parity_vs_oracle": parity,
             "gpu_launches": int(launches),
             "clocks": clk, "roofline": roofline, "roofline_compress": roofline_c, "cpu_baseline": cpu,
             "e2e": e2e,
@@ -575,7 +610,7 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0 if all_ok else 1
+    return 0 if all_ok and (parity is None or parity["equal"]) else 1
 
 
 if __name__ == "__main__":

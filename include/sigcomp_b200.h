@@ -80,9 +80,12 @@ SC_API int sc_model_create(int device, int32_t window, int32_t emb_dim, int32_t 
 /* Release the model and every device buffer it owns. */
 SC_API int sc_model_destroy(sc_model *model);
 
-/* Select the MLP implementation: 0 = automatic (tcgen05 when the geometry allows),
+/* Select the MLP implementation: 0 = automatic (the tcgen05 kernels: fused persistent
+ * kernels on SM pairs for compress/decompress, the tcgen05 layer kernels for
+ * sc_mlp_logits_device; a model they cannot run is refused with SC_ERR_UNSUPPORTED),
  * 1 = tcgen05 fused persistent kernels on SM pairs (cta_group::2), 2 = CUDA-core
- * kernels, 3 = tcgen05 one launch per layer, 4 = tcgen05 fused on single SMs. */
+ * kernels, 3 = tcgen05 one launch per layer, 4 = tcgen05 fused on single SMs.
+ * Paths 2-4 are cross-checks of the same arithmetic, run only when selected here. */
 SC_API int sc_model_set_mlp_path(sc_model *model, int32_t path);
 
 /*
@@ -133,6 +136,34 @@ SC_API int sc_decompress_chunks_device(sc_model *model, const uint32_t *words, c
  */
 SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t rows, int8_t *logits,
                          void *stream);
+
+/*
+ * The range coder alone on given int8 logits (no MLP), in device memory.  Replaces the
+ * reference's step encoder, GpuRangeStepEncoder (sigcomp/gpu_entropy_coding.py:255-303:
+ * encode_step_int8 at every step, then seal and get_compressed), with the byte-exact
+ * semantics of the CPU coder (sigcomp/cpu_entropy_coding.py:90-227: _frequencies,
+ * _encode_one, _seal).
+ *   logits         int8  [offsets[n_streams]][256]   the model's logits of every coded step
+ *   symbols        uint8 [offsets[n_streams]]        the symbols to code
+ *   offsets        int64 [n_streams + 1]             stream c codes rows offsets[c] .. offsets[c+1]
+ *                                                    (each at most the model's chunk_len)
+ *   words, words_capacity, word_offsets, stream_errors   as in sc_compress_chunks
+ */
+SC_API int sc_encode_logits_device(sc_model *model, const int8_t *logits, const uint8_t *symbols,
+                                   const int64_t *offsets, int64_t n_streams, uint32_t *words,
+                                   int64_t words_capacity, int64_t *word_offsets, uint8_t *stream_errors,
+                                   void *stream);
+
+/*
+ * Inverse: decode offsets[c+1] - offsets[c] symbols of stream c, step t using logits row
+ * offsets[c] + t.  Replaces GpuRangeDecoder (sigcomp/gpu_entropy_coding.py:400-454,
+ * decode_step_int8 at every step; semantics of CpuRangeDecoder and _decode_partition,
+ * cpu_entropy_coding.py:230-266, 451-481).  Device memory; stream_errors as in
+ * sc_decompress_chunks (SC_ERR_CORRUPT_STREAM names the first invalid stream).
+ */
+SC_API int sc_decode_logits_device(sc_model *model, const int8_t *logits, const int64_t *offsets,
+                                   const uint32_t *words, const int64_t *word_offsets, int64_t n_streams,
+                                   uint8_t *symbols, uint8_t *stream_errors, void *stream);
 
 /*
  * SigComp's signal split on the device: _split_signal (sigcomp/main.py:504-521)

@@ -78,11 +78,17 @@ typedef struct {
     int64_t inverted;
     uint32_t first;
     int64_t position;
+    /* coverage counters for the tests (no effect on the output): carry episodes (inverted
+       set to 1), the longest run of inverted words, whether the seal flushed inverted words
+       and whether it emitted the extra zero word */
+    int64_t cov_episodes, cov_longest;
+    int cov_seal_flush, cov_seal_zero;
 } sco_encoder;
 
 void sco_encoder_init(sco_encoder *e)
 {
     e->lower = 0; e->range = ~(uint64_t)0; e->inverted = 0; e->first = 0; e->position = 0;
+    e->cov_episodes = 0; e->cov_longest = 0; e->cov_seal_flush = 0; e->cov_seal_zero = 0;
 }
 
 /* returns 0 on success, 1 when the output capacity would be exceeded */
@@ -117,7 +123,9 @@ int sco_encode_symbol(sco_encoder *e, const int64_t *freqs, int symbol,
         } else {
             e->inverted = 1;
             e->first = lower_word;
+            e->cov_episodes += 1;
         }
+        if (e->inverted > e->cov_longest) e->cov_longest = e->inverted;
     }
     return 0;
 }
@@ -129,6 +137,7 @@ int sco_seal(sco_encoder *e, uint32_t *out, int64_t capacity)
         uint64_t point = e->lower + 0xFFFFFFFFull;
         if (e->inverted > 0) {
             uint64_t emit_first, emit_rest;
+            e->cov_seal_flush = 1;
             if (point < e->lower) { emit_first = (uint64_t)e->first + 1; emit_rest = 0; }
             else { emit_first = e->first; emit_rest = 0xFFFFFFFFull; }
             if (e->position >= capacity) return 1;
@@ -145,6 +154,7 @@ int sco_seal(sco_encoder *e, uint32_t *out, int64_t capacity)
         if (upper_word == point_word) {
             if (e->position >= capacity) return 1;
             out[e->position++] = 0;
+            e->cov_seal_zero = 1;
         }
     }
     return 0;
@@ -163,6 +173,29 @@ int sco_encode_chunk(const int8_t *logits, const uint8_t *symbols, int64_t T,
     }
     int rc = sco_seal(&e, out, capacity);
     *nwords = e.position;
+    return rc;
+}
+
+/* sco_encode_chunk that also reports which carry paths the stream took:
+   cov[0] carry episodes, cov[1] longest inverted run, cov[2] seal flushed inverted words,
+   cov[3] seal emitted the extra zero word. */
+int sco_encode_chunk_coverage(const int8_t *logits, const uint8_t *symbols, int64_t T, const int64_t *lut,
+                              uint32_t *out, int64_t capacity, int64_t *nwords, int64_t *cov)
+{
+    sco_encoder e;
+    int64_t freqs[SCO_VOCAB];
+    int rc = 0;
+    sco_encoder_init(&e);
+    for (int64_t t = 0; t < T && !rc; ++t) {
+        sco_frequencies(logits + t * SCO_VOCAB, lut, freqs);
+        rc = sco_encode_symbol(&e, freqs, symbols[t], out, capacity);
+    }
+    if (!rc) rc = sco_seal(&e, out, capacity);
+    *nwords = e.position;
+    cov[0] = e.cov_episodes;
+    cov[1] = e.cov_longest;
+    cov[2] = e.cov_seal_flush;
+    cov[3] = e.cov_seal_zero;
     return rc;
 }
 

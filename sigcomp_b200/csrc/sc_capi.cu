@@ -34,6 +34,11 @@ int split_signal_device(sc_model *m, const int16_t *samples, const int64_t *off_
                         int64_t n_reads, int lsb, int16_t *sig0, uint8_t *small, int64_t *small_off,
                         uint16_t *large, uint32_t *large_pos, int64_t *large_off, cudaStream_t s);
 int wait_selftest(cudaStream_t s, int *done_d);
+int encode_logits_device(sc_model *m, const int8_t *logits, const uint8_t *symbols, const int64_t *off_d,
+                         const int64_t *off_h, int64_t n, uint32_t *words, int64_t words_capacity,
+                         int64_t *word_offsets, uint8_t *errors_d, cudaStream_t s);
+void decode_logits_device(sc_model *m, const int8_t *logits, const int64_t *off_d, int64_t n, const uint32_t *words,
+                          const int64_t *word_offsets, uint8_t *symbols, uint8_t *errors_d, cudaStream_t s);
 int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *off_d, int64_t n_reads, int lsb,
                              const uint8_t *small, const int64_t *small_off, const uint16_t *large,
                              const uint32_t *large_pos, const int64_t *large_off, int16_t *samples,
@@ -257,7 +262,7 @@ int sc_model_destroy(sc_model *m)
         }
         for (DevBuf *b : {&m->ws_windows, &m->ws_act0, &m->ws_act1, &m->ws_logits, &m->ws_pairs, &m->ws_stage,
                           &m->ws_nwords, &m->ws_err, &m->ws_scan, &m->ws_tmp, &m->ws_order, &m->ws_state,
-                          &m->ws_tok_off, &m->ws_misc, &m->ws_ering})
+                          &m->ws_tok_off, &m->ws_misc, &m->ws_ering, &m->ws_sched})
             b->release();
     }
     delete m;
@@ -612,6 +617,94 @@ int sc_mlp_logits_device(sc_model *m, const int16_t *windows, int64_t rows, int8
     return guarded(m, [&]() -> int {
         run_mlp(m, windows, rows, logits, s);
         SC_CUDA(cudaStreamSynchronize(s));
+        return SC_OK;
+    });
+}
+
+int sc_encode_logits_device(sc_model *m, const int8_t *logits, const uint8_t *symbols, const int64_t *offsets,
+                            int64_t n_streams, uint32_t *words, int64_t words_capacity, int64_t *word_offsets,
+                            uint8_t *stream_errors, void *stream)
+{
+    g_err[0] = 0;
+    if (!m || n_streams < 0 || (n_streams > 0 && (!offsets || !words || !word_offsets))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        std::vector<int64_t> off_h(n_streams + 1);
+        SC_CUDA(cudaMemcpyAsync(off_h.data(), offsets, sizeof(int64_t) * (n_streams + 1), cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        int rc = check_offsets(m, off_h.data(), n_streams);
+        if (rc) return rc;
+        if (off_h[n_streams] > 0 && (!logits || !symbols)) {
+            set_error("invalid argument");
+            return SC_ERR_INVALID_ARGUMENT;
+        }
+        if (n_streams == 0) {
+            const int64_t zero = 0;
+            SC_CUDA(cudaMemcpyAsync(word_offsets, &zero, sizeof(zero), cudaMemcpyHostToDevice, s));
+            SC_CUDA(cudaStreamSynchronize(s));
+            return SC_OK;
+        }
+        uint8_t *d_err = stream_errors ? stream_errors : (uint8_t *)m->ws_tmp.get((size_t)n_streams + 16, s);
+        int r = encode_logits_device(m, logits, symbols, offsets, off_h.data(), n_streams, words, words_capacity,
+                                     word_offsets, d_err, s);
+        if (r == 2) return SC_ERR_CAPACITY;
+        std::vector<uint8_t> errs(n_streams);
+        SC_CUDA(cudaMemcpyAsync(errs.data(), d_err, (size_t)n_streams, cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        const int bad = first_error(errs.data(), n_streams);
+        if (bad >= 0) {
+            set_error("range-coder output capacity exceeded in stream %d; increase max_words", bad);
+            return SC_ERR_CAPACITY;
+        }
+        return SC_OK;
+    });
+}
+
+int sc_decode_logits_device(sc_model *m, const int8_t *logits, const int64_t *offsets, const uint32_t *words,
+                            const int64_t *word_offsets, int64_t n_streams, uint8_t *symbols,
+                            uint8_t *stream_errors, void *stream)
+{
+    g_err[0] = 0;
+    if (!m || n_streams < 0 || (n_streams > 0 && (!offsets || !word_offsets))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    if (n_streams == 0) return SC_OK;
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        std::vector<int64_t> off_h(n_streams + 1), woff_h(n_streams + 1);
+        SC_CUDA(cudaMemcpyAsync(off_h.data(), offsets, sizeof(int64_t) * (n_streams + 1), cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaMemcpyAsync(woff_h.data(), word_offsets, sizeof(int64_t) * (n_streams + 1),
+                                cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        if (off_h[0] != 0) {
+            set_error("offsets[0] must be 0");
+            return SC_ERR_INVALID_ARGUMENT;
+        }
+        for (int64_t c = 0; c < n_streams; ++c) {
+            const int64_t len = off_h[c + 1] - off_h[c], nw = woff_h[c + 1] - woff_h[c];
+            if (len < 0 || nw < 0 || (len > 0) != (nw > 0)) {
+                set_error("Invalid range-coded chunk for its token length");
+                return SC_ERR_INVALID_ARGUMENT;
+            }
+        }
+        if ((off_h[n_streams] > 0 && (!logits || !symbols)) || (woff_h[n_streams] > 0 && !words)) {
+            set_error("invalid argument");
+            return SC_ERR_INVALID_ARGUMENT;
+        }
+        uint8_t *d_err = stream_errors ? stream_errors : (uint8_t *)m->ws_tmp.get((size_t)n_streams + 16, s);
+        decode_logits_device(m, logits, offsets, n_streams, words, word_offsets, symbols, d_err, s);
+        std::vector<uint8_t> errs(n_streams);
+        SC_CUDA(cudaMemcpyAsync(errs.data(), d_err, (size_t)n_streams, cudaMemcpyDeviceToHost, s));
+        SC_CUDA(cudaStreamSynchronize(s));
+        const int bad = first_error(errs.data(), n_streams);
+        if (bad >= 0) {
+            set_error("invalid range stream or mismatching entropy model in stream %d", bad);
+            return SC_ERR_CORRUPT_STREAM;
+        }
         return SC_OK;
     });
 }

@@ -153,29 +153,19 @@ __global__ void k_windows_decode(const uint8_t *__restrict__ tokens, const int64
     win[idx] = s < 0 ? (int16_t)SC_SOS : (int16_t)tokens[tok_off[order[i]] + s];
 }
 
-__global__ void __launch_bounds__(256) k_decode_step(const int8_t *__restrict__ logits, const uint64_t *__restrict__ lut,
-                                                     const uint32_t *__restrict__ words,
-                                                     const int64_t *__restrict__ order,
-                                                     const int64_t *__restrict__ tok_off, int64_t n_act, int64_t t,
-                                                     DecState *__restrict__ st, uint8_t *__restrict__ tokens,
-                                                     uint8_t *__restrict__ errors)
+// One range-decoder step of one chunk by a whole warp (_decode_partition,
+// cpu_entropy_coding.py:230-266): the exact frequency table of the row's 256 logits, the
+// symbol whose interval holds the quotient, and the state update with renormalisation.
+// Every lane holds the same state and ends with the same symbol.  Returns false (state
+// untouched) for a stream that does not fit the model: zero scale or quotient >= 2^24.
+__device__ __forceinline__ bool warp_decode_step(const int8_t *__restrict__ row, const uint64_t *lut_s,
+                                                 const uint32_t *__restrict__ words, DecState &d, int &sym)
 {
-    __shared__ uint64_t lut_s[SC_VOCAB];
-    for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = lut[i];
-    __syncthreads();
     const int lane = threadIdx.x & 31;
-    const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (i >= n_act) return;
-    const int64_t c = order[i];
-    if (errors[c]) return;
-    DecState d = st[i];
     const uint64_t scale = d.range >> SC_PRECISION;
     const uint64_t q = scale ? (d.point - d.lower) / scale : ~0ull;
-    if (scale == 0 || q >= (uint64_t)SC_TOTAL) {
-        if (lane == 0) errors[c] = 1;
-        return;
-    }
-    const uint2 raw = *reinterpret_cast<const uint2 *>(logits + i * SC_VOCAB + lane * 8);
+    if (scale == 0 || q >= (uint64_t)SC_TOTAL) return false;
+    const uint2 raw = *reinterpret_cast<const uint2 *>(row + lane * 8);
     int8_t x[8];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -210,23 +200,77 @@ __global__ void __launch_bounds__(256) k_decode_step(const int8_t *__restrict__ 
     int total = cnt;
 #pragma unroll
     for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    const int sym = total - 1;
+    sym = total - 1;
     const int owner = sym >> 3;
     const uint32_t s_cum = __shfl_sync(0xffffffffu, my_cum, owner);
     const uint32_t s_f = __shfl_sync(0xffffffffu, my_f, owner);
+    d.lower += scale * (uint64_t)s_cum;
+    d.range = scale * (uint64_t)s_f;
+    if (d.range < (1ull << 32)) {
+        d.lower <<= 32;
+        d.range <<= 32;
+        d.point <<= 32;
+        if (d.read_pos < d.end_pos) d.point |= words[d.read_pos];
+        d.read_pos += 1;
+    }
+    return true;
+}
+
+__global__ void __launch_bounds__(256) k_decode_step(const int8_t *__restrict__ logits, const uint64_t *__restrict__ lut,
+                                                     const uint32_t *__restrict__ words,
+                                                     const int64_t *__restrict__ order,
+                                                     const int64_t *__restrict__ tok_off, int64_t n_act, int64_t t,
+                                                     DecState *__restrict__ st, uint8_t *__restrict__ tokens,
+                                                     uint8_t *__restrict__ errors)
+{
+    __shared__ uint64_t lut_s[SC_VOCAB];
+    for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = lut[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t i = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (i >= n_act) return;
+    const int64_t c = order[i];
+    if (errors[c]) return;
+    DecState d = st[i];
+    int sym;
+    if (!warp_decode_step(logits + i * SC_VOCAB, lut_s, words, d, sym)) {
+        if (lane == 0) errors[c] = 1;
+        return;
+    }
     if (lane == 0) {
-        d.lower += scale * (uint64_t)s_cum;
-        d.range = scale * (uint64_t)s_f;
-        if (d.range < (1ull << 32)) {
-            d.lower <<= 32;
-            d.range <<= 32;
-            d.point <<= 32;
-            if (d.read_pos < d.end_pos) d.point |= words[d.read_pos];
-            d.read_pos += 1;
-        }
         st[i] = d;
         tokens[tok_off[c] + t] = (uint8_t)sym;
     }
+}
+
+// The range decoder alone on given logits: one warp per stream, all of its steps in turn;
+// step t of stream c takes logits row off[c] + t and writes symbols[off[c] + t].
+__global__ void __launch_bounds__(256) k_decode_logits(const int8_t *__restrict__ logits,
+                                                       const int64_t *__restrict__ off,
+                                                       const uint32_t *__restrict__ words,
+                                                       const int64_t *__restrict__ word_off, int64_t n,
+                                                       const uint64_t *__restrict__ lut,
+                                                       uint8_t *__restrict__ symbols, uint8_t *__restrict__ errors)
+{
+    __shared__ uint64_t lut_s[SC_VOCAB];
+    for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = lut[i];
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t c = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (c >= n) return;
+    const int64_t b = off[c], len = off[c + 1] - b;
+    DecState d;
+    dec_init(d, words, word_off[c], word_off[c + 1]);
+    uint8_t err = 0;
+    for (int64_t t = 0; t < len; ++t) {
+        int sym;
+        if (!warp_decode_step(logits + (b + t) * SC_VOCAB, lut_s, words, d, sym)) {
+            err = 1;
+            break;
+        }
+        if (lane == 0) symbols[b + t] = (uint8_t)sym;
+    }
+    if (lane == 0) errors[c] = err;
 }
 
 inline unsigned blocks_for(int64_t n, int per) { return (unsigned)((n + per - 1) / per); }
@@ -392,25 +436,11 @@ int decompress_device(sc_model *m, const uint32_t *words, const int64_t *word_of
         return 1;
     }
     if (use_tc(m) && fused_supported(m)) {
-        // persistent decoding: every launch keeps its chunks resident for all steps;
-        // chunks are split evenly over as few launches as the kernel's capacity allows
-        const int64_t cap = fused_decode_capacity(m);
-        const int64_t launches = (n + cap - 1) / cap;
-        const int64_t per = (n + launches - 1) / launches;
-        std::vector<int32_t> maxlen;
-        for (int64_t g0 = 0; g0 < n; g0 += per) {
-            const int64_t g1 = std::min(n, g0 + per);
-            if (sorted_len[g0] == 0) break;          // the rest are empty chunks
-            maxlen.clear();
-            int64_t work = 0;
-            for (int64_t j = g0; j < g1; j += 128) maxlen.push_back((int32_t)sorted_len[j]);
-            for (int64_t j = g0; j < g1; ++j) work += sorted_len[j];
-            int32_t *d_maxlen = (int32_t *)m->ws_windows.get(sizeof(int32_t) * maxlen.size(), s);
-            SC_CUDA(cudaMemcpyAsync(d_maxlen, maxlen.data(), sizeof(int32_t) * maxlen.size(), cudaMemcpyHostToDevice, s));
-            fused_decode(m, order_d + g0, g1 - g0, d_maxlen, lengths_d, st + g0, words, tokens, tok_off_d, errors_d,
-                         work, s);
-            SC_CUDA(cudaStreamSynchronize(s));       // tile lengths are rebuilt for the next launch
-        }
+        // persistent decoding of every nonempty chunk (empty ones sort last)
+        int64_t n_live = n;
+        while (n_live > 0 && sorted_len[n_live - 1] == 0) --n_live;
+        fused_decode(m, order_d, n_live, sorted_len.data(), lengths_d, st, words, tokens, tok_off_d, errors_d, s);
+        SC_CUDA(cudaStreamSynchronize(s));
         return 0;
     }
     const int64_t max_rows = max_rows_per_pass(m);
@@ -451,6 +481,62 @@ int decompress_device(sc_model *m, const uint32_t *words, const int64_t *word_of
     }
     SC_CUDA(cudaStreamSynchronize(s));
     return 0;
+}
+
+// The range encoder alone on given logits (k_cdf_select -> k_encode -> scan -> k_compact):
+// stream c codes symbols[off[c] .. off[c+1]) with the frequencies of the same logits rows.
+int encode_logits_device(sc_model *m, const int8_t *logits, const uint8_t *symbols, const int64_t *off_d,
+                         const int64_t *off_h, int64_t n, uint32_t *words, int64_t words_capacity,
+                         int64_t *word_offsets, uint8_t *errors_d, cudaStream_t s)
+{
+    const int64_t cap = (int64_t)m->chunk_len + 32;
+    const int64_t rows = off_h[n];
+    k_set_i64<<<1, 1, 0, s>>>(word_offsets, 0);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    int *overflow = (int *)m->ws_misc.get(64, s);
+    SC_CUDA(cudaMemsetAsync(overflow, 0, sizeof(int), s));
+    int64_t *nw = (int64_t *)m->ws_nwords.get(sizeof(int64_t) * n * 2, s);
+    int64_t *incl = nw + n;
+    uint32_t *stage = (uint32_t *)m->ws_stage.get(sizeof(uint32_t) * n * cap, s);
+    uint2 *pairs = (uint2 *)m->ws_pairs.get(sizeof(uint2) * std::max<int64_t>(rows, 1), s);
+    if (rows > 0) {
+        k_cdf_select<<<(unsigned)std::min<int64_t>(blocks_for(rows, 8), 148 * 16), 256, 0, s>>>(logits, symbols,
+                                                                                                 m->lut, rows, pairs);
+        SC_LAUNCH_CHECK();
+        count_launch();
+    }
+    k_encode<<<blocks_for(n, 128), 128, 0, s>>>(pairs, off_d, 0, n, 0, stage, cap, nw, errors_d);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    size_t tmp_bytes = 0;
+    SC_CUDA(cub::DeviceScan::InclusiveSum(nullptr, tmp_bytes, nw, incl, (int)n, s));
+    void *tmp = m->ws_scan.get(tmp_bytes, s);
+    SC_CUDA(cub::DeviceScan::InclusiveSum(tmp, tmp_bytes, nw, incl, (int)n, s));
+    count_launch();
+    k_compact<<<blocks_for(n * 32, 256), 256, 0, s>>>(stage, cap, nw, incl, n, 0, word_offsets, words,
+                                                      words_capacity, overflow);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    int h_overflow = 0;
+    SC_CUDA(cudaMemcpyAsync(&h_overflow, overflow, sizeof(int), cudaMemcpyDeviceToHost, s));
+    SC_CUDA(cudaStreamSynchronize(s));
+    if (h_overflow) {
+        set_error("output words capacity %lld is too small", (long long)words_capacity);
+        return 2;
+    }
+    return 0;
+}
+
+// The range decoder alone on given logits (k_decode_logits).
+void decode_logits_device(sc_model *m, const int8_t *logits, const int64_t *off_d, int64_t n, const uint32_t *words,
+                          const int64_t *word_offsets, uint8_t *symbols, uint8_t *errors_d, cudaStream_t s)
+{
+    k_decode_logits<<<blocks_for(n, 8), 256, 0, s>>>(logits, off_d, words, word_offsets, n, m->lut, symbols,
+                                                     errors_d);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    SC_CUDA(cudaStreamSynchronize(s));
 }
 
 }  // namespace sc

@@ -161,13 +161,15 @@ void mlp_tc_prepare(sc_model *m);
 
 // Fused persistent kernels (all layers + coder step in one launch).
 bool fused_supported(const sc_model *m);
-int64_t fused_decode_capacity(const sc_model *m);
 void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_t0, int64_t n_tiles,
                     const uint8_t *tokens, const int64_t *tok_off, int64_t row_base, int64_t rows, uint2 *pairs,
                     cudaStream_t s);
-void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32_t *tile_maxlen,
+// Decode the chunks order[0 .. n_rows), sorted by length (descending, all nonzero; their
+// lengths on the host in sorted_len), with every layer and the decoder step in persistent
+// kernels: one launch on SM pairs, or launches of at most the single-SM kernels' capacity.
+void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int64_t *sorted_len,
                   const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
-                  const int64_t *out_off, uint8_t *errors, int64_t work_rows, cudaStream_t s);
+                  const int64_t *out_off, uint8_t *errors, cudaStream_t s);
 
 // Value of the device error flag set by timed-out waits (optionally cleared).
 int read_device_error(int clear);
@@ -194,5 +196,5 @@ struct sc_model {
     int trace_cap = 0;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
-        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering;
+        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering, ws_sched;
 };

@@ -31,6 +31,16 @@ namespace sc {
 constexpr int KT2 = 6;                // the larger of the two: sizes per-slot arrays
 template <bool DECODE> constexpr int kt2() { return DECODE ? 6 : 5; }
 
+// Decoder schedule.  Every SM pair runs KT2 tile lanes (slots); a lane decodes its queue of
+// pair-tiles back to back, the next pair-tile starting at the global step after the previous
+// one's last.  The host cuts each pair's timeline into segments over which no lane changes
+// pair-tile, so one launch decodes any number of chunks.
+struct DecSeg {
+    int32_t s0, s1;                   // global steps [s0, s1) of this pair
+    int32_t pt[KT2];                  // pair-tile of each lane, -1 while the lane is idle
+    int32_t start[KT2];               // global step of that pair-tile's step 0
+};
+
 struct Fused2Params {
     CUtensorMap w[FMAX_LAYERS];       // weights, box 128 rows x 128 B (half of a 256-row unit)
     CUtensorMap act[2];               // activation ping-pong, box 128 x 128 B
@@ -60,7 +70,8 @@ struct Fused2Params {
     int64_t ering_sos_row;            // first row of the start-of-sequence block
     const int64_t *order;
     int64_t n_rows;
-    const int32_t *tile_maxlen;
+    const DecSeg *segs;               // this launch's segments, pair after pair
+    const int32_t *pair_seg;          // [pairs + 1]: segments of pair i are segs[pair_seg[i] .. pair_seg[i+1])
     const int64_t *lengths;
     DecState *state;
     const uint32_t *words;
@@ -90,7 +101,7 @@ struct F2Cfg {
     static constexpr int OFF_BIAS = OFF_X + X_BYTES;
     static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
-    static constexpr int NBAR = 2 * STAGES + 8;
+    static constexpr int NBAR = 2 * STAGES + 9;     // ... + the teardown drain barrier
     static constexpr int OFF_CNT = OFF_BAR + NBAR * 8;
     static constexpr int OFF_TMEM = OFF_CNT + 8 * 4;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;
@@ -227,40 +238,49 @@ __device__ __forceinline__ void row_find_cached(uint32_t taddr, const uint64_t *
     }
 }
 
-// Walk this pair's units in the fixed order both CTAs and every role follow.
-// Pair-tile pt covers tiles 2*pt (rank 0) and 2*pt+1 (rank 1).
+// Walk this pair's units in the fixed order both CTAs and every role follow, calling
+// f(gs, tt, pt, step, L, nh) for each unit: layer L, output half nh, of pair-tile pt in slot tt
+// at that tile's step `step`.  Pair-tile pt covers tiles 2*pt (rank 0) and 2*pt+1 (rank 1).
+//   decode: gs is the pair's global step; every slot's lane runs its pair-tiles back to back,
+//           so slot tt's units of global step gs are its (gs * NL + L)-th layer completion
+//   compress: gs is the group of up to kt2() tiles; every tile takes one step
 template <bool DECODE, typename F>
 __device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
 {
     const int NP = gridDim.x / 2;
     const int pair = blockIdx.x / 2;
+    const int NL = p.num_layers;
+    if (DECODE) {
+        for (int sg = p.pair_seg[pair]; sg < p.pair_seg[pair + 1]; ++sg) {
+            const DecSeg *S = p.segs + sg;
+            const int s1 = S->s1;
+            for (int gs = S->s0; gs < s1; ++gs)
+                for (int L = 0; L < NL; ++L)
+#pragma unroll 1
+                    for (int tt = 0; tt < KT2; ++tt) {
+                        const int pt = S->pt[tt];
+                        if (pt < 0) continue;
+                        const int step = gs - S->start[tt];
+                        const int NH = p.out_dim[L] / TN;
+                        for (int nh = 0; nh < NH; ++nh)
+                            if (!f(gs, tt, pt, step, L, nh)) return;
+                    }
+        }
+        return;
+    }
     const int n_pt = (p.n_tiles + 1) / 2;
     const int my_pt = n_pt > pair ? (n_pt - 1 - pair) / NP + 1 : 0;
-    const int NL = p.num_layers;
     constexpr int KTD = kt2<DECODE>();
     for (int g0 = 0, grp = 0; g0 < my_pt; g0 += KTD, ++grp) {
         const int gn = min(KTD, my_pt - g0);
-        int maxlen[KT2];
-        int steps = 1;
-#pragma unroll
-        for (int tt = 0; tt < KT2; ++tt) {
-            maxlen[tt] = 0;
-            if (tt < gn) {
-                // tiles are ordered by decreasing length: a pair-tile lasts as long as its first tile
-                maxlen[tt] = DECODE ? p.tile_maxlen[2 * (pair + (g0 + tt) * NP)] : 1;
-                steps = max(steps, maxlen[tt]);
-            }
-        }
-        for (int step = 0; step < steps; ++step)
-            for (int L = 0; L < NL; ++L)
+        for (int L = 0; L < NL; ++L)
 #pragma unroll 1
-                for (int tt = 0; tt < gn; ++tt) {
-                    if (DECODE && maxlen[tt] <= step) continue;
-                    const int pt = pair + (g0 + tt) * NP;
-                    const int NH = p.out_dim[L] / TN;
-                    for (int nh = 0; nh < NH; ++nh)
-                        if (!f(grp, tt, pt, step, L, nh)) return;
-                }
+            for (int tt = 0; tt < gn; ++tt) {
+                const int pt = pair + (g0 + tt) * NP;
+                const int NH = p.out_dim[L] / TN;
+                for (int nh = 0; nh < NH; ++nh)
+                    if (!f(grp, tt, pt, 0, L, nh)) return;
+            }
     }
 }
 
@@ -282,6 +302,8 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
     uint64_t *full = bars, *empty = bars + C::STAGES;
     uint64_t *acc_full = bars + 2 * C::STAGES, *acc_empty = acc_full + 2;
     uint64_t *g_full = acc_empty + 2, *g_empty = g_full + 2;
+    // drain: the MMA issuer's last commit (both CTAs); TMEM is freed only after it
+    uint64_t *drain = g_empty + 2;
     // act_cnt[tt]: +1 per epilogue warp of this CTA when its tile of slot tt finishes a
     // layer; completion number k is reached at act_cnt[tt] >= EPI_WARPS * (k + 1)
     uint32_t *act_cnt = (uint32_t *)(smem + C::OFF_CNT);
@@ -304,6 +326,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             mbar_init(&g_full[b], 4);
             mbar_init(&g_empty[b], 1);
         }
+        mbar_init(drain, 1);
         for (int tt = 0; tt < 8; ++tt) act_cnt[tt] = 0;
         fence_mbar_init();
     }
@@ -325,27 +348,28 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         if (lane == 0) {
             // ---- TMA producer (both CTAs): own activation rows + own half of the weights
             uint32_t it = 0;
+            bool aborted = false;
             // the embedding ring (hundreds of MB) streams from DRAM: keep it from evicting
             // the weights and activations that live in L2
             const uint64_t ring_policy = l2_policy_evict_first();
-            for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
                 if (DECODE && L == 0 && nh == 1) return true;       // loaded with half 0
                 const int nkb = p.in_dim[L] / KB;
-                trace_ev(p, 0, 0, L, nh, tt, step);
+                trace_ev(p, 0, 0, L, nh, tt, gs);
                 if (nh == 0 && (L >= 1 || (DECODE && step > 0))) {
                     // layer L-1 of this tile is written (decode layer 0: the previous step's
                     // last layer appended its token to the embedding ring)
-                    const uint32_t k = (uint32_t)((DECODE ? step : grp) * NL + L - 1);
-                    if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return false;
+                    const uint32_t k = (uint32_t)(gs * NL + L - 1);
+                    if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return !(aborted = true);
                 }
-                trace_ev(p, 0, 1, L, nh, tt, step);
+                trace_ev(p, 0, 1, L, nh, tt, gs);
                 const int ring0 = (blockIdx.x * kt2<DECODE>() + tt) * WIN * TM;
                 // compress layer 0 reads A from the sliding buffer: its stages carry the
                 // weights of two K blocks (the second in the unused activation half)
                 const int kstep = (!DECODE && L == 0) ? 2 : 1;
                 for (int kb = 0; kb < nkb; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
-                    if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return false;
+                    if (!mbar_wait_cluster(&empty[s], ((it / C::STAGES) & 1) ^ 1)) return !(aborted = true);
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(&full[s], 0);
                     const bool a_tma = DECODE || L != 0;
@@ -365,24 +389,38 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
-                trace_ev(p, 0, 2, L, nh, tt, step);
+                trace_ev(p, 0, 2, L, nh, tt, gs);
                 return true;
             });
+            if (aborted) {
+                // Abort path: loads this CTA issued may still be landing in its shared memory.
+                // They complete on the leader's full barrier, and a stage is released (empty)
+                // only after the MMA that read it, so the leader waits for the full phases and
+                // the peer for the empty phases of the last STAGES stages it issued (bounded),
+                // then both give copies that no barrier reports on time to land.
+                for (uint32_t i = it > (uint32_t)C::STAGES ? it - C::STAGES : 0; i < it; ++i) {
+                    const int s = i % C::STAGES;
+                    const uint32_t ph = (i / C::STAGES) & 1;
+                    if (rank == 0) mbar_wait_cluster_drain(&full[s], ph);
+                    else mbar_wait_cluster_drain(&empty[s], ph);
+                }
+                spin_ns(100000);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0 && rank == 0) {
             // ---- MMA issuer (leader CTA only)
             uint32_t it = 0, uu = 0, li = 0;
-            for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
                 // decoding layer 0: half 1 accumulates in the other buffer during half 0's pass
                 if (DECODE && L == 0 && nh == 1) return true;
                 const bool dual = DECODE && L == 0;
                 const int nkb = p.in_dim[L] / KB;
                 const int ab = uu & 1;
-                trace_ev(p, 1, 0, L, nh, tt, step);
+                trace_ev(p, 1, 0, L, nh, tt, gs);
                 if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
                 if (dual && !mbar_wait_cluster(&acc_empty[ab ^ 1], (((uu + 1) >> 1) & 1) ^ 1)) return false;
-                trace_ev(p, 1, 1, L, nh, tt, step);
+                trace_ev(p, 1, 1, L, nh, tt, gs);
                 const int gb = li & 1;
                 if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
                 tc_fence_after();
@@ -391,7 +429,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 for (int kb = 0; kb < nkb; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
-                    if (L == 0 && kb < 4) trace_ev(p, 1, 3, L, kb, tt, step);
+                    if (L == 0 && kb < 4) trace_ev(p, 1, 3, L, kb, tt, gs);
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
                     if (kstep == 2) {
@@ -406,7 +444,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 mma_commit_pair(&acc_full[ab], 0x3);
                 if (dual) mma_commit_pair(&acc_full[ab ^ 1], 0x3);
-                trace_ev(p, 1, 2, L, nh, tt, step);
+                trace_ev(p, 1, 2, L, nh, tt, gs);
                 uu += dual ? 2 : 1;
                 if (!DECODE && L == 0 && nh == p.out_dim[0] / TN - 1) {
                     mma_commit_pair(&g_empty[gb], 0x3);
@@ -414,7 +452,11 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 return true;
             });
+            // completes (in both CTAs) once every MMA issued above, and every commit before
+            // it, has completed: normal end or abort alike
+            mma_commit_pair(drain, 0x3);
         }
+        __syncwarp();
     } else if (warp >= 2 && warp < 2 + EPI_WARPS) {
         // ---- epilogue warps: TMEM lane quarter q; hidden layers split the eight
         // 32-column chunks of a unit between the EPI_PER_Q warps of a quarter.  The last
@@ -425,13 +467,13 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         const int part = (warp - 2) >> 2;
         const int r = q * 32 + lane;
         uint32_t uu = 0, lu = 0;
-        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
             const int ab = uu & 1;
             const bool tr = warp == 2 && lane == 0;
-            if (tr) trace_ev(p, 2, 0, L, nh, tt, step);
+            if (tr) trace_ev(p, 2, 0, L, nh, tt, gs);
             bool mine = false;
             if (L == NL - 1) {
-                mine = DECODE ? ((tt + grp) % EPI_PER_Q == part) : ((int)(lu % EPI_PER_Q) == part);
+                mine = DECODE ? (tt % EPI_PER_Q == part) : ((int)(lu % EPI_PER_Q) == part);
                 ++lu;
             }
             // decoding: this row's coder state and quotient, fetched before the logits are ready
@@ -455,9 +497,18 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
             }
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[ab], (uu >> 1) & 1))) return false;
-            if (tr) trace_ev(p, 2, 1, L, nh, tt, step);
+            if (tr) trace_ev(p, 2, 1, L, nh, tt, gs);
             ++uu;
             tc_fence_after();
+            const int NH = p.out_dim[L] / TN;
+            if (L >= 1 && nh == NH - 1) {
+                // every MMA that reads this tile's layer-L input has completed: its rows are
+                // dead until layer L+1 overwrites them, so drop them from L2 instead of
+                // letting them be written back to DRAM (each warp of the quarter takes every
+                // third 128-byte line of its rows)
+                const int8_t *in_row = p.act_ptr[(L - 1) & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N;
+                for (int ln = part; ln < p.in_dim[L] / 128; ln += EPI_PER_Q) discard_l2_line(in_row + ln * 128);
+            }
             const uint32_t taddr = tmem_base + ab * TN + ((uint32_t)(q * 32) << 16);
             const Requant rq = p.rq[L];
             // fast-path parameters as scalars (uniform per unit)
@@ -470,6 +521,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             if (L < NL - 1) {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
                 // requantise chunk c (32 columns) of this row and store it to the activations
+                // with one 32-byte store
                 auto store_chunk = [&](const uint32_t (&va)[32], int c) {
                     const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
                     uint32_t packed[8];
@@ -480,9 +532,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
 #pragma unroll
                         for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
                     }
-                    uint4 *dst = reinterpret_cast<uint4 *>(dst_row + c * 32);
-                    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-                    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+                    st_global_v8(dst_row + c * 32, packed);
                 };
                 // chunks part, part + 3 and (parts 0 and 1) part + 6: each chunk's TMEM load is
                 // issued before the previous chunk is requantised, and the accumulator is
@@ -505,12 +555,12 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 if (lane == 0) mbar_arrive_cluster_relaxed(acc_empty_leader);
                 if (three) store_chunk(va, c2);
                 else store_chunk(vb, c1);
-                if (nh == p.out_dim[L] / TN - 1) {
+                if (nh == NH - 1) {
                     fence_proxy_async_global();
                     __syncwarp();
                     if (lane == 0) counter_add_release(&act_cnt[tt], 1);
                 }
-                if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
+                if (tr) trace_ev(p, 2, 2, L, nh, tt, gs);
                 return true;
             }
             if (mine) {
@@ -582,7 +632,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 mbar_arrive_cluster_relaxed(acc_empty_leader);
                 counter_add_release(&act_cnt[tt], 1);
             }
-            if (tr) trace_ev(p, 2, 2, L, nh, tt, step);
+            if (tr) trace_ev(p, 2, 2, L, nh, tt, gs);
             return true;
         });
     } else if (!DECODE) {
@@ -590,7 +640,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         const int tw = threadIdx.x - 32 * (2 + EPI_WARPS);   // 0..63
         const int j = tw & 7, r0 = tw >> 3;
         uint32_t li = 0;
-        for_each_unit2<DECODE>(p, [&](int grp, int tt, int pt, int step, int L, int nh) -> bool {
+        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
             if (L != 0 || nh != 0) return true;
             const int gb = li & 1;
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&g_empty[gb], ((li >> 1) & 1) ^ 1))) return false;
@@ -615,6 +665,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             return true;
         });
     }
+    // Teardown.  Every MMA has completed once the drain barrier's phase 0 does (the issuer's
+    // last commit, after all its MMAs and commits); only then is TMEM freed.  The wait is
+    // bounded: on a timeout the device error flag is already set by the role that gave up.
+    if (warp == 1) mbar_wait_cluster_drain(drain, 0);
     tc_fence_before();
     __syncthreads();
     cluster_sync();                       // no CTA leaves while its peer may still signal it

@@ -19,6 +19,9 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <array>
+#include <climits>
+#include <queue>
 
 #include "sc_internal.h"
 #include "sc_tc.cuh"
@@ -469,10 +472,6 @@ bool fused_supported(const sc_model *m) { return m->tc_ok && m->num_layers <= FM
 
 static bool use_pairs(const sc_model *m) { return m->mlp_path != 4 && m->num_sms >= 2; }
 
-int64_t fused_decode_capacity(const sc_model *m)
-{
-    return use_pairs(m) ? (int64_t)(m->num_sms / 2) * kt2<true>() * 2 * TM : (int64_t)m->num_sms * KT * TM;
-}
 
 static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s)
 {
@@ -562,18 +561,95 @@ __global__ void k_sos_block(int8_t *dst, const int8_t *emb)
         reinterpret_cast<const int4 *>(emb + (size_t)SC_SOS * EMB_DIM)[threadIdx.x & (EMB_DIM / 16 - 1)];
 }
 
-void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32_t *tile_maxlen,
+// The decoder schedule of one launch on SM pairs (see DecSeg).  Pair-tile i holds rows
+// 256 i .. 256 i + 255 of the length-sorted order and lasts as many steps as its first row.
+// Pair-tiles go, longest first, to the pair with the least total steps so far (ties: the
+// lowest pair) and, within it, to the lane with the fewest steps (ties: the lowest lane), so
+// pairs finish together and each keeps its six lanes busy for as long as it can.  Each pair's
+// timeline is then cut at every step where a lane changes pair-tile.
+struct DecSchedule {
+    std::vector<DecSeg> segs;
+    std::vector<int32_t> pair_seg;
+};
+
+static DecSchedule build_decode_schedule(const std::vector<int32_t> &pt_len, int pairs)
+{
+    const int n_pt = (int)pt_len.size();
+    std::vector<int64_t> pair_load(pairs, 0);
+    std::vector<std::array<int64_t, KT2>> lane_load(pairs);
+    std::vector<std::array<std::vector<int32_t>, KT2>> queue(pairs);
+    for (auto &l : lane_load) l.fill(0);
+    // min-heap on (steps so far, pair)
+    std::priority_queue<std::pair<int64_t, int>, std::vector<std::pair<int64_t, int>>, std::greater<>> heap;
+    for (int i = 0; i < pairs; ++i) heap.push({0, i});
+    for (int pt = 0; pt < n_pt; ++pt) {
+        const auto top = heap.top();
+        heap.pop();
+        const int pr = top.second;
+        int lane = 0;
+        for (int t = 1; t < KT2; ++t)
+            if (lane_load[pr][t] < lane_load[pr][lane]) lane = t;
+        queue[pr][lane].push_back(pt);
+        lane_load[pr][lane] += pt_len[pt];
+        pair_load[pr] += pt_len[pt];
+        heap.push({pair_load[pr], pr});
+    }
+    DecSchedule out;
+    out.pair_seg.push_back(0);
+    for (int pr = 0; pr < pairs; ++pr) {
+        int idx[KT2] = {};
+        int32_t start[KT2] = {};
+        int32_t gs = 0;
+        while (true) {
+            int32_t next = INT32_MAX;
+            for (int t = 0; t < KT2; ++t)
+                if (idx[t] < (int)queue[pr][t].size())
+                    next = std::min(next, start[t] + pt_len[queue[pr][t][idx[t]]]);
+            if (next == INT32_MAX) break;
+            DecSeg sg;
+            sg.s0 = gs;
+            sg.s1 = next;
+            for (int t = 0; t < KT2; ++t) {
+                const bool on = idx[t] < (int)queue[pr][t].size();
+                sg.pt[t] = on ? queue[pr][t][idx[t]] : -1;
+                sg.start[t] = on ? start[t] : 0;
+            }
+            out.segs.push_back(sg);
+            for (int t = 0; t < KT2; ++t)
+                if (idx[t] < (int)queue[pr][t].size() && start[t] + pt_len[queue[pr][t][idx[t]]] == next) {
+                    ++idx[t];
+                    start[t] = next;
+                }
+            gs = next;
+        }
+        out.pair_seg.push_back((int32_t)out.segs.size());
+    }
+    return out;
+}
+
+void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int64_t *sorted_len,
                   const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
-                  const int64_t *out_off, uint8_t *errors, int64_t work_rows, cudaStream_t s)
+                  const int64_t *out_off, uint8_t *errors, cudaStream_t s)
 {
     if (n_rows <= 0) return;
     const int64_t n_tiles = (n_rows + TM - 1) / TM;
-    ProfScope ps(m->prof, KK_FUSED_DECODE, s, work_rows);
     if (use_pairs(m)) {
+        // one launch for the whole batch: every pair-tile is queued on a lane of some SM pair
         const int64_t n_pt = (n_tiles + 1) / 2;
-        const int grid = 2 * (int)std::min<int64_t>(n_pt, m->num_sms / 2);
-        if (n_pt > (int64_t)(grid / 2) * kt2<true>())
-            throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        if (n_pt > INT32_MAX / 2) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        std::vector<int32_t> pt_len(n_pt);
+        int64_t work = 0;
+        for (int64_t i = 0; i < n_pt; ++i) pt_len[i] = (int32_t)sorted_len[i * 2 * TM];
+        for (int64_t j = 0; j < n_rows; ++j) work += sorted_len[j];
+        const int pairs = (int)std::min<int64_t>(n_pt, m->num_sms / 2);
+        const int grid = 2 * pairs;
+        const DecSchedule sched = build_decode_schedule(pt_len, pairs);
+        const size_t seg_bytes = sizeof(DecSeg) * sched.segs.size();
+        uint8_t *sd = (uint8_t *)m->ws_sched.get(seg_bytes + sizeof(int32_t) * sched.pair_seg.size(), s);
+        SC_CUDA(cudaMemcpyAsync(sd, sched.segs.data(), seg_bytes, cudaMemcpyHostToDevice, s));
+        SC_CUDA(cudaMemcpyAsync(sd + seg_bytes, sched.pair_seg.data(), sizeof(int32_t) * sched.pair_seg.size(),
+                                cudaMemcpyHostToDevice, s));
+        ProfScope ps(m->prof, KK_FUSED_DECODE, s, work);
         Fused2Params p{};
         fused2_common(m, p, grid, s);
         // embedding ring: [grid][kt2][WIN] blocks of 128 rows x 128 B, then the SOS block
@@ -588,7 +664,8 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
         p.n_tiles = (int)n_tiles;
         p.order = order;
         p.n_rows = n_rows;
-        p.tile_maxlen = tile_maxlen;
+        p.segs = reinterpret_cast<const DecSeg *>(sd);
+        p.pair_seg = reinterpret_cast<const int32_t *>(sd + seg_bytes);
         p.lengths = lengths;
         p.state = state;
         p.words = words;
@@ -596,25 +673,44 @@ void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int32
         p.out_off = out_off;
         p.errors = errors;
         launch_pairs<true>(p, grid, s);
-    } else {
-        const int grid = (int)std::min<int64_t>(n_tiles, m->num_sms);
-        if (n_tiles > (int64_t)grid * KT) throw CudaError{cudaErrorInvalidValue, "fused_decode: too many rows"};
+        SC_LAUNCH_CHECK();
+        count_launch();
+        return;
+    }
+    // single-SM kernels (a cross-check path): launches of at most grid * KT tiles, chunks split
+    // evenly over as few launches as that capacity allows
+    const int64_t cap = (int64_t)m->num_sms * KT * TM;
+    const int64_t launches = (n_rows + cap - 1) / cap;
+    const int64_t per = (n_rows + launches - 1) / launches;
+    std::vector<int32_t> maxlen;
+    for (int64_t g0 = 0; g0 < n_rows; g0 += per) {
+        const int64_t g1 = std::min(n_rows, g0 + per);
+        maxlen.clear();
+        int64_t work = 0;
+        for (int64_t j = g0; j < g1; j += TM) maxlen.push_back((int32_t)sorted_len[j]);
+        for (int64_t j = g0; j < g1; ++j) work += sorted_len[j];
+        int32_t *d_maxlen = (int32_t *)m->ws_sched.get(sizeof(int32_t) * maxlen.size(), s);
+        SC_CUDA(cudaMemcpyAsync(d_maxlen, maxlen.data(), sizeof(int32_t) * maxlen.size(), cudaMemcpyHostToDevice, s));
+        const int64_t g_tiles = (g1 - g0 + TM - 1) / TM;
+        ProfScope ps(m->prof, KK_FUSED_DECODE, s, work);
+        const int grid = (int)std::min<int64_t>(g_tiles, m->num_sms);
         FusedParams p{};
         fused_common(m, p, grid, s);
-        p.n_tiles = (int)n_tiles;
-        p.order = order;
-        p.n_rows = n_rows;
-        p.tile_maxlen = tile_maxlen;
+        p.n_tiles = (int)g_tiles;
+        p.order = order + g0;
+        p.n_rows = g1 - g0;
+        p.tile_maxlen = d_maxlen;
         p.lengths = lengths;
-        p.state = state;
+        p.state = state + g0;
         p.words = words;
         p.tokens_out = tokens_out;
         p.out_off = out_off;
         p.errors = errors;
         k_fused<true><<<grid, 256, FCfg<true>::SMEM, s>>>(p);
+        SC_LAUNCH_CHECK();
+        count_launch();
+        SC_CUDA(cudaStreamSynchronize(s));       // tile lengths are rebuilt for the next launch
     }
-    SC_LAUNCH_CHECK();
-    count_launch();
 }
 
 namespace {

@@ -157,6 +157,23 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     }
 }
 
+// Waits of the abort path (a role gave up and is draining its own asynchronous work before
+// the CTA ends): shorter limit, and no new error code (the first timeout already set one).
+constexpr uint64_t kDrainLimitNs = 50000000ull;
+
+__device__ __forceinline__ bool mbar_wait_cluster_drain(uint64_t *bar, uint32_t parity) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait_cluster(bar, parity))
+        if (globaltimer_ns() - t0 > kDrainLimitNs) return false;
+    return true;
+}
+
+// Idle for `ns` nanoseconds (abort path: lets copies already issued land before the CTA ends).
+__device__ __forceinline__ void spin_ns(uint64_t ns) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < ns) __nanosleep(256);
+}
+
 __device__ __forceinline__ void cluster_sync() {
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
@@ -204,6 +221,20 @@ __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
 // generic-proxy shared-memory writes -> visible to the async proxy (MMA/TMA)
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---- global stores and L2 ------------------------------------------------------
+// One 32-byte store (st.global.v8.b32, sm_100): `dst` must be 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void *dst, const uint32_t (&v)[8]) {
+    asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(dst), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+                 "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
+}
+
+// Drop a 128-byte line from L2 without writing it back (its contents become undefined): for
+// data that no one reads again before it is next written.  `p` must be 128-byte aligned.
+__device__ __forceinline__ void discard_l2_line(const void *p) {
+    asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
 }
 
 // ---- tcgen05 ----------------------------------------------------------------

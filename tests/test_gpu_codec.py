@@ -271,3 +271,34 @@ def test_large_round_trip_properties(lossless_model):
         codec.set_mlp_path("auto")
     bits = 8 * sum(len(f) for f in framed) / sum(lengths)
     assert 4.0 < bits < 8.0
+
+
+def test_decoder_runs_several_tiles_per_lane(lossless_model):
+    """More chunks than the SM pairs' lanes hold at once (74 pairs x 6 lanes x 256 rows): one
+    persistent launch decodes them all, each lane taking its next pair-tile when the previous
+    one ends, with chunk lengths varying inside and across tiles.  Streams against the oracle
+    on a sample, every chunk by round trip."""
+    from oracle import signal
+    from sigcomp_b200 import _lib, synthetic
+    L = 64
+    reads = synthetic.make_reads("r10_lognormal", seed=9, count=300)
+    toks = np.concatenate([signal.split_signal(r)[1] for r in reads])
+    rng = np.random.default_rng(3)
+    lens = rng.integers(0, L + 1, size=160000)
+    lens[rng.random(len(lens)) < 0.5] = L                 # half of them full, like real batches
+    off = np.zeros(len(lens) + 1, np.int64)
+    np.cumsum(lens, out=off[1:])
+    assert off[-1] <= len(toks)
+    tokens = toks[:off[-1]]
+    codec = _codec(lossless_model, chunk_len=L)
+    words, woff = codec.compress_flat(tokens, off)
+    sample = list(range(0, len(lens), 997))
+    chunks = [tokens[off[i]:off[i + 1]] for i in sample]
+    ref = OracleModel(lossless_model).compress_chunks(chunks, chunk_len=L, backend="int_mm")
+    assert [words[woff[i]:woff[i + 1]].astype("<u4").tobytes() for i in sample] == ref
+    launches = _lib.kernel_launches()
+    back = codec.decompress_flat(words, woff, lens)
+    assert np.array_equal(back, tokens)
+    # the persistent decoder is one launch (plus the start-of-sequence block and the
+    # decoder-state set-up), whatever the number of chunks
+    assert _lib.kernel_launches() - launches <= 4
