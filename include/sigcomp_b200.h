@@ -254,8 +254,10 @@ SC_API int sc_profile_read(sc_model *model, int32_t kind, double *total_ms, int6
  * %globaltimer (ns), word 1 packs role | event << 4 | layer << 8 | half << 12 |
  * slot << 16 | step << 32 (roles 0 producer, 1 MMA, 2 epilogue, 3 layer-0
  * builders; events 0 begin, 1 dependency satisfied, 2 end).  0 disables.
- * sc_trace_read copies up to `capacity` records of CTA 0 or 1 of the most
- * recent launch and returns their number (-1 on error).
+ * The records of a CTA are split evenly over the four roles (each role keeps
+ * at most records_per_cta / 4).  sc_trace_read copies up to `capacity` records
+ * of CTA 0 or 1 of the most recent launch, role after role, and returns their
+ * number (-1 on error).
  */
 SC_API int sc_trace_enable(sc_model *model, int32_t records_per_cta);
 SC_API int64_t sc_trace_read(sc_model *model, int32_t cta, uint64_t *records, int64_t capacity);

@@ -493,8 +493,8 @@ int sc_trace_enable(sc_model *m, int32_t records_per_cta)
         m->trace_cap = 0;
         if (records_per_cta > 0) {
             SC_CUDA(cudaMalloc(&m->trace_buf, sizeof(unsigned long long) * 2 * 2 * (size_t)records_per_cta));
-            SC_CUDA(cudaMalloc(&m->trace_count, 2 * sizeof(unsigned int)));
-            SC_CUDA(cudaMemset(m->trace_count, 0, 2 * sizeof(unsigned int)));
+            SC_CUDA(cudaMalloc(&m->trace_count, 8 * sizeof(unsigned int)));
+            SC_CUDA(cudaMemset(m->trace_count, 0, 8 * sizeof(unsigned int)));
             m->trace_cap = records_per_cta;
         }
         return SC_OK;
@@ -506,12 +506,17 @@ int64_t sc_trace_read(sc_model *m, int32_t cta, uint64_t *records, int64_t capac
     if (!m || cta < 0 || cta > 1 || !m->trace_buf) return 0;
     int64_t n = 0;
     int rc = guarded(m, [&]() -> int {
-        unsigned int cnt[2] = {0, 0};
+        // per role, the records it wrote (a role's region holds trace_cap / 4 of them)
+        unsigned int cnt[8] = {};
         SC_CUDA(cudaMemcpy(cnt, m->trace_count, sizeof(cnt), cudaMemcpyDeviceToHost));
-        n = std::min<int64_t>(std::min<int64_t>(cnt[cta], m->trace_cap), capacity);
-        if (n > 0)
-            SC_CUDA(cudaMemcpy(records, m->trace_buf + (size_t)cta * m->trace_cap * 2, sizeof(uint64_t) * 2 * n,
-                               cudaMemcpyDeviceToHost));
+        const int64_t per_role = m->trace_cap / 4;
+        for (int role = 0; role < 4 && n < capacity; ++role) {
+            const int64_t k = std::min<int64_t>(std::min<int64_t>(cnt[cta * 4 + role], per_role), capacity - n);
+            if (k > 0)
+                SC_CUDA(cudaMemcpy(records + 2 * n, m->trace_buf + ((size_t)cta * 4 + role) * per_role * 2,
+                                   sizeof(uint64_t) * 2 * k, cudaMemcpyDeviceToHost));
+            n += k;
+        }
         return SC_OK;
     });
     return rc == SC_OK ? n : -1;

@@ -53,9 +53,10 @@ struct Fused2Params {
     const int8_t *emb;
     const uint64_t *lut;
     int n_tiles;
-    // optional unit trace of the first CTA pair (null when tracing is off)
-    unsigned long long *trace;        // [2][trace_cap][2]
-    unsigned int *trace_count;        // [2]
+    // optional unit trace of the first CTA pair (null when tracing is off): per CTA, one region
+    // of trace_cap / 4 records for each of the roles 0-3
+    unsigned long long *trace;        // [2][4][trace_cap / 4][2]
+    unsigned int *trace_count;        // [2][4]: records each role wrote
     int trace_cap;
     // compress
     const int32_t *tile_chunk;
@@ -111,15 +112,40 @@ struct F2Cfg {
 // Trace record of one role event for a unit (first CTA pair only):
 // word 0 = %globaltimer, word 1 = role | event << 4 | L << 8 | nh << 12 | tt << 16 | step << 32.
 // roles: 0 producer, 1 MMA, 2 epilogue (warp 2), 3 compress layer-0 builders
-__device__ __forceinline__ void trace_ev(const Fused2Params &p, int role, int ev, int L, int nh, int tt, int step)
+// Each role traces from one thread into its own region of the trace buffer.  The producer and
+// MMA threads count their records in a register (`n`), so a record costs them two stores and no
+// global atomic on their critical path; the epilogue's tracing lane counts with an atomic on its
+// role's global counter, which needs no register for the count across its unit loop.
+__device__ __forceinline__ void trace_put(const Fused2Params &p, int role, unsigned int i, int ev, int L, int nh,
+                                          int tt, int step)
 {
-    if (p.trace == nullptr || blockIdx.x >= 2) return;
-    const unsigned int i = atomicAdd(p.trace_count + blockIdx.x, 1u);
-    if (i >= (unsigned int)p.trace_cap) return;
-    unsigned long long *r = p.trace + ((size_t)blockIdx.x * p.trace_cap + i) * 2;
+    if (i >= (unsigned int)p.trace_cap / 4) return;
+    unsigned long long *r = p.trace + (((size_t)blockIdx.x * 4 + role) * (p.trace_cap / 4) + i) * 2;
     r[0] = globaltimer_ns();
     r[1] = (unsigned long long)role | ((unsigned long long)ev << 4) | ((unsigned long long)L << 8) |
            ((unsigned long long)nh << 12) | ((unsigned long long)tt << 16) | ((unsigned long long)step << 32);
+}
+
+// Both are compiled out of the untraced kernels (TRACE false), which are the ones a normal
+// call launches: the trace code would otherwise cost registers in every kernel.
+template <bool TRACE>
+__device__ __forceinline__ void trace_ev(const Fused2Params &p, unsigned int &n, int role, int ev, int L, int nh,
+                                         int tt, int step)
+{
+    if constexpr (TRACE) {
+        if (blockIdx.x >= 2) return;
+        trace_put(p, role, n++, ev, L, nh, tt, step);
+    }
+}
+
+template <bool TRACE>
+__device__ __forceinline__ void trace_ev_atomic(const Fused2Params &p, int role, int ev, int L, int nh, int tt,
+                                                int step)
+{
+    if constexpr (TRACE) {
+        if (blockIdx.x >= 2) return;
+        trace_put(p, role, atomicAdd(p.trace_count + blockIdx.x * 4 + role, 1u), ev, L, nh, tt, step);
+    }
 }
 
 // Row frequency statistics (_frequencies, cpu_entropy_coding.py:90-110) from the
@@ -292,7 +318,9 @@ __device__ __forceinline__ void mma_k_block_pair(uint32_t d, uint32_t a_addr, ui
                     (!first || k) ? 1u : 0u);
 }
 
-template <bool DECODE>
+// TRACE: the instrumented build of the kernel (sc_trace_enable), with the unit trace of the
+// first SM pair; normal calls launch the build without it.
+template <bool DECODE, bool TRACE>
 __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_constant__ Fused2Params p)
 {
     using C = F2Cfg<DECODE>;
@@ -348,6 +376,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         if (lane == 0) {
             // ---- TMA producer (both CTAs): own activation rows + own half of the weights
             uint32_t it = 0;
+            unsigned int tn = 0;                       // trace records written
             bool aborted = false;
             // the embedding ring (hundreds of MB) streams from DRAM: keep it from evicting
             // the weights and activations that live in L2
@@ -355,14 +384,14 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
                 if (DECODE && L == 0 && nh == 1) return true;       // loaded with half 0
                 const int nkb = p.in_dim[L] / KB;
-                trace_ev(p, 0, 0, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 0, 0, L, nh, tt, gs);
                 if (nh == 0 && (L >= 1 || (DECODE && step > 0))) {
                     // layer L-1 of this tile is written (decode layer 0: the previous step's
                     // last layer appended its token to the embedding ring)
                     const uint32_t k = (uint32_t)(gs * NL + L - 1);
                     if (!counter_wait(&act_cnt[tt], EPI_WARPS * (k + 1))) return !(aborted = true);
                 }
-                trace_ev(p, 0, 1, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 0, 1, L, nh, tt, gs);
                 const int ring0 = (blockIdx.x * kt2<DECODE>() + tt) * WIN * TM;
                 // compress layer 0 reads A from the sliding buffer: its stages carry the
                 // weights of two K blocks (the second in the unused activation half)
@@ -389,9 +418,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
-                trace_ev(p, 0, 2, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 0, 2, L, nh, tt, gs);
                 return true;
             });
+            if (TRACE && blockIdx.x < 2) p.trace_count[blockIdx.x * 4 + 0] = tn;
             if (aborted) {
                 // Abort path: loads this CTA issued may still be landing in its shared memory.
                 // They complete on the leader's full barrier, and a stage is released (empty)
@@ -411,16 +441,17 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         if (lane == 0 && rank == 0) {
             // ---- MMA issuer (leader CTA only)
             uint32_t it = 0, uu = 0, li = 0;
+            unsigned int tn = 0;                       // trace records written
             for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
                 // decoding layer 0: half 1 accumulates in the other buffer during half 0's pass
                 if (DECODE && L == 0 && nh == 1) return true;
                 const bool dual = DECODE && L == 0;
                 const int nkb = p.in_dim[L] / KB;
                 const int ab = uu & 1;
-                trace_ev(p, 1, 0, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 1, 0, L, nh, tt, gs);
                 if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
                 if (dual && !mbar_wait_cluster(&acc_empty[ab ^ 1], (((uu + 1) >> 1) & 1) ^ 1)) return false;
-                trace_ev(p, 1, 1, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 1, 1, L, nh, tt, gs);
                 const int gb = li & 1;
                 if (!DECODE && L == 0 && nh == 0 && !mbar_wait_cluster(&g_full[gb], (li >> 1) & 1)) return false;
                 tc_fence_after();
@@ -429,7 +460,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 for (int kb = 0; kb < nkb; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
-                    if (L == 0 && kb < 4) trace_ev(p, 1, 3, L, kb, tt, gs);
+                    if (L == 0 && kb < 4) trace_ev<TRACE>(p, tn, 1, 3, L, kb, tt, gs);
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
                     if (kstep == 2) {
@@ -444,7 +475,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 mma_commit_pair(&acc_full[ab], 0x3);
                 if (dual) mma_commit_pair(&acc_full[ab ^ 1], 0x3);
-                trace_ev(p, 1, 2, L, nh, tt, gs);
+                trace_ev<TRACE>(p, tn, 1, 2, L, nh, tt, gs);
                 uu += dual ? 2 : 1;
                 if (!DECODE && L == 0 && nh == p.out_dim[0] / TN - 1) {
                     mma_commit_pair(&g_empty[gb], 0x3);
@@ -452,6 +483,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 return true;
             });
+            if (TRACE && blockIdx.x < 2) p.trace_count[blockIdx.x * 4 + 1] = tn;
             // completes (in both CTAs) once every MMA issued above, and every commit before
             // it, has completed: normal end or abort alike
             mma_commit_pair(drain, 0x3);
@@ -470,7 +502,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
             const int ab = uu & 1;
             const bool tr = warp == 2 && lane == 0;
-            if (tr) trace_ev(p, 2, 0, L, nh, tt, gs);
+            if (tr) trace_ev_atomic<TRACE>(p, 2, 0, L, nh, tt, gs);
             bool mine = false;
             if (L == NL - 1) {
                 mine = DECODE ? (tt % EPI_PER_Q == part) : ((int)(lu % EPI_PER_Q) == part);
@@ -497,7 +529,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
             }
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&acc_full[ab], (uu >> 1) & 1))) return false;
-            if (tr) trace_ev(p, 2, 1, L, nh, tt, gs);
+            if (tr) trace_ev_atomic<TRACE>(p, 2, 1, L, nh, tt, gs);
             ++uu;
             tc_fence_after();
             const int NH = p.out_dim[L] / TN;
@@ -560,7 +592,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     __syncwarp();
                     if (lane == 0) counter_add_release(&act_cnt[tt], 1);
                 }
-                if (tr) trace_ev(p, 2, 2, L, nh, tt, gs);
+                if (tr) trace_ev_atomic<TRACE>(p, 2, 2, L, nh, tt, gs);
                 return true;
             }
             if (mine) {
@@ -616,12 +648,19 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                         }
                         p.state[drow] = s;
                         p.tokens_out[p.out_off[dc] + step] = (uint8_t)sym;
-                        // append the token's embedding row to this row's window ring
-                        const int4 *e = reinterpret_cast<const int4 *>(p.emb + sym * EMB_DIM);
-                        int4 *dst = reinterpret_cast<int4 *>(
+                        // append the token's embedding row to this row's window ring; the ring is
+                        // read back only 1 to 64 steps later, long after L2 would have to keep it,
+                        // so the append goes out with the evict-first policy
+                        const uint4 *e = reinterpret_cast<const uint4 *>(p.emb + sym * EMB_DIM);
+                        uint8_t *dst = reinterpret_cast<uint8_t *>(
                             p.ering_ptr + (((size_t)(blockIdx.x * kt2<DECODE>() + tt) * WIN + (step & (WIN - 1))) * TM + r) * KB);
+                        const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
-                        for (int i = 0; i < KB / 16; ++i) dst[i] = e[i];
+                        for (int i = 0; i < KB / 32; ++i) {
+                            const uint4 a = e[2 * i], b = e[2 * i + 1];
+                            const uint32_t v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                            st_global_v8_hint(dst + 32 * i, v, pol);
+                        }
                     }
                     fence_proxy_async_global();          // the ring block is read by TMA next step
                 }
@@ -632,7 +671,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 mbar_arrive_cluster_relaxed(acc_empty_leader);
                 counter_add_release(&act_cnt[tt], 1);
             }
-            if (tr) trace_ev(p, 2, 2, L, nh, tt, gs);
+            if (tr) trace_ev_atomic<TRACE>(p, 2, 2, L, nh, tt, gs);
             return true;
         });
     } else if (!DECODE) {

@@ -399,8 +399,10 @@ void mlp_tc_prepare(sc_model *m)
     set_smem_attr<A_GATHER>();
     set_smem_attr<A_SLIDE>();
     SC_CUDA(cudaFuncSetAttribute(k_fused<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FCfg<true>::SMEM));
-    SC_CUDA(cudaFuncSetAttribute(k_fused2<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<true>::SMEM));
-    SC_CUDA(cudaFuncSetAttribute(k_fused2<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<false>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<true>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<false>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<true>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_fused2<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, F2Cfg<false>::SMEM));
     auto &maps2 = m->tc_wmaps2;
     maps2.clear();
     for (auto &L : m->layers) maps2.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, TN / 2));
@@ -493,7 +495,7 @@ static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s
     p.emb = m->emb;
     p.lut = m->lut;
     if (m->trace_cap > 0) {
-        SC_CUDA(cudaMemsetAsync(m->trace_count, 0, 2 * sizeof(unsigned int), s));
+        SC_CUDA(cudaMemsetAsync(m->trace_count, 0, 8 * sizeof(unsigned int), s));
         p.trace = m->trace_buf;
         p.trace_count = m->trace_count;
         p.trace_cap = m->trace_cap;
@@ -515,7 +517,8 @@ static void launch_pairs(const Fused2Params &p, int grid, cudaStream_t s)
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    SC_CUDA(cudaLaunchKernelEx(&cfg, k_fused2<DECODE>, p));
+    if (p.trace != nullptr) SC_CUDA(cudaLaunchKernelEx(&cfg, k_fused2<DECODE, true>, p));
+    else SC_CUDA(cudaLaunchKernelEx(&cfg, k_fused2<DECODE, false>, p));
 }
 
 void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_t0, int64_t n_tiles,

@@ -231,6 +231,13 @@ __device__ __forceinline__ void st_global_v8(void *dst, const uint32_t (&v)[8]) 
                  : "memory");
 }
 
+// The same with an L2 cache policy (l2_policy_evict_first and the like).
+__device__ __forceinline__ void st_global_v8_hint(void *dst, const uint32_t (&v)[8], uint64_t policy) {
+    asm volatile("st.global.L2::cache_hint.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8}, %9;" ::"l"(dst), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "l"(policy)
+                 : "memory");
+}
+
 // Drop a 128-byte line from L2 without writing it back (its contents become undefined): for
 // data that no one reads again before it is next written.  `p` must be 128-byte aligned.
 __device__ __forceinline__ void discard_l2_line(const void *p) {
