@@ -3,17 +3,20 @@
 
 Metric: compress & decompress Msamples/s at 1/2/4/8 B200, with
 bits/sample, bit-exact.  A step is one compress + decompress round trip of a
-batch of synthetic int16 reads drawn from the configuration-2 generator
-(R10.4.1-like, lognormal lengths, median 30,000 samples) with the bundled
-lossless model and chunk_len 2048, the SigComp per-read path on the device:
+rank's share of a job of synthetic int16 reads with the bundled model and
+chunk_len 2048, the SigComp per-read path on the device, one sub-batch of reads
+at a time (SigComp too codes a shard in batches):
 
   compress    split every read (sc_split_signal_device: delta / zig-zag / split of
               main.py:504-521) -> chunk the token streams -> sc_compress_chunks_device
   decompress  sc_decompress_chunks_device -> sc_reassemble_signal_device -> int16 reads
 
-Each rank holds its own batch (weak scaling, reads sharded by rank, no collective
-on the data path); after each compress the ranks exchange their stream byte
-counts (all-gather of one int64), which is how a sharded run lays out the archive.
+The job is sharded as SigComp's multi-GPU driver shards it: contiguous read ranges
+balanced by sample count (sharding.sample_balanced_ranges, read_assignment.py:14-49),
+every rank coding its range alone; the only collective is the all-gather of every
+rank's stream byte count that lays out the archive (sharding.exchange_shard_bytes).
+Configuration 2 (the default) is weak scaling: the job holds 20,000 reads per GPU.
+Configuration 5 is strong scaling: one 200,000-read job (~11 G samples) over N GPUs.
 
   value      whole-job round-trip Msamples/s with the reads resident in HBM
   e2e        the same with every step's reads copied in from pinned host memory,
@@ -29,7 +32,8 @@ counts (all-gather of one int64), which is how a sharded run lays out the archiv
 
 `--impl reference` times that CPU port alone on the host cores.  `--workload` picks
 another BASELINE configuration (config1: the 64-read CPU case, config3: RNA004-like
-reads, config4: the lossy mode with lsb_eliminate 3); configuration 2 is the default.
+reads, config4: the lossy mode with lsb_eliminate 3, config5: the 200,000-read
+strong-scaling job); configuration 2 is the default.
 """
 
 import argparse
@@ -51,21 +55,28 @@ CHUNK_LEN = 2048
 L2_BYTES = 126 * 1024 * 1024           # B200 L2
 # int8 MLP work per coded token: 2 x (8192*512 + 7*512*512 + 512*256) multiply-adds
 OPS_PER_TOKEN = 2 * (8192 * 512 + 7 * 512 * 512 + 512 * 256)
-# BASELINE.json configurations: (generator, reads, model, lossy lsb, description).  Configuration 2 is
-# the headline; 1 is the CPU-runnable case, 3 the RNA004-like set (no RNA004 model is bundled: the
-# lossless R10.4.1 model codes it), 4 the lossy mode on configuration 2's reads.
+# BASELINE.json configurations: (generator, reads, model, lossy lsb, description, scaling).  `reads`
+# is per GPU for weak scaling and the whole job for strong scaling.  Configuration 2 is the headline;
+# 1 is the CPU-runnable case, 3 the RNA004-like set (no RNA004 model is bundled: the lossless
+# R10.4.1 model codes it), 4 the lossy mode on configuration 2's reads, 5 the multi-GPU job.
 WORKLOADS = {
     "config1": ("r10_config1", 64, "lossless", 0,
-                "r10_config1 (64 reads x 20,000 samples, levels N(500,60), dwell 12, noise 12), lossless model"),
+                "r10_config1 (64 reads x 20,000 samples, levels N(500,60), dwell 12, noise 12), lossless model",
+                "weak"),
     "config2": ("r10_lognormal", 20000, "lossless", 0,
                 "r10_lognormal (configuration 2 generator: lognormal lengths median 30,000, levels N(500,60), "
-                "dwell 12, noise 12), lossless model"),
+                "dwell 12, noise 12), lossless model", "weak"),
     "config3": ("rna_lognormal", 10000, "lossless", 0,
                 "rna_lognormal (configuration 3 generator: lognormal lengths median 15,000, levels N(800,90), "
-                "dwell 30, noise 20), lossless R10.4.1 model (no RNA004 model is bundled)"),
+                "dwell 30, noise 20), lossless R10.4.1 model (no RNA004 model is bundled)", "weak"),
     "config4": ("r10_lognormal", 20000, "lossy", 3,
-                "r10_lognormal (configuration 2 reads), lossy model, lsb_eliminate 3"),
+                "r10_lognormal (configuration 2 reads), lossy model, lsb_eliminate 3", "weak"),
+    "config5": ("r10_lognormal_large", 200000, "lossless", 0,
+                "r10_lognormal_large (configuration 5: 200,000 reads, lognormal lengths median 40,000, "
+                "levels N(500,60), dwell 12, noise 12), lossless model, one job sharded by read", "strong"),
 }
+JOB_SEED = 1000             # seed of every job's read lengths and, with the read index, of its samples
+SUB_SAMPLES = 1_500_000_000  # samples per sub-batch of a rank's reads (bounds the device buffers)
 
 
 def parse_args():
@@ -77,7 +88,14 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2",
                     help="BASELINE configuration (config2, the headline, by default)")
     ap.add_argument("--reads", type=int, default=None,
-                    help="reads per GPU per step (default: the configuration's read count)")
+                    help="reads per GPU (weak scaling) or of the whole job (strong scaling); default: the "
+                         "configuration's")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default=None,
+                    help="override the configuration's scaling mode")
+    ap.add_argument("--sub-samples", type=int, default=SUB_SAMPLES,
+                    help="samples per sub-batch of a rank's reads")
+    ap.add_argument("--gen-workers", type=int, default=None,
+                    help="host processes generating the synthetic reads (default: the host's cores / ranks)")
     ap.add_argument("--cpu-reads", type=int, default=32,
                     help="reads in the CPU baseline sample (about 1.6 M samples: 10-20 s of CPU work per "
                          "warm-up + round trip)")
@@ -90,8 +108,9 @@ def parse_args():
                     help="tokens per chunk (2048 in every configuration; smaller values give short "
                          "decoder launches for profiling)")
     args = ap.parse_args()
-    gen, count, model, lsb, desc = WORKLOADS[args.workload]
+    gen, count, model, lsb, desc, scaling = WORKLOADS[args.workload]
     args.generator, args.model, args.lsb, args.workload_desc = gen, model, lsb, desc
+    args.scaling = args.scaling or scaling
     if args.reads is None:
         args.reads = count
     return args
@@ -109,13 +128,51 @@ def lossy_round_trip(x, lsb):
     return ((v & ~(step - 1)) + ((v >> (lsb - 1)) & 1) * step).astype(np.int16)
 
 
-def make_reads(rank, n_reads, generator="r10_lognormal"):
-    """One rank's batch of int16 reads: (reads, concatenated samples, sample offsets)."""
+def job_plan(generator, reads, scaling, world):
+    """The job's read lengths and every rank's read range: the job holds `reads` reads per rank
+    (weak) or `reads` in all (strong), cut by sample count as SigComp's multi-GPU driver cuts it."""
+    from sigcomp_b200 import sharding, synthetic
+    n_job = reads * world if scaling == "weak" else reads
+    lengths = synthetic.job_lengths(generator, JOB_SEED, n_job)
+    plans = sharding.sample_balanced_ranges(lengths, world)
+    plans = list(plans) + [sharding.SampleRange(n_job, n_job, 0)] * (world - len(plans))
+    return lengths, plans
+
+
+def _gen_part(args):
+    generator, lengths, start, stop = args
     from sigcomp_b200 import synthetic
-    reads = synthetic.make_reads(generator, seed=1000 + rank, count=n_reads)
-    off = np.zeros(len(reads) + 1, dtype=np.int64)
-    np.cumsum([len(r) for r in reads], out=off[1:])
-    return reads, np.concatenate(reads), off
+    return synthetic.job_reads(generator, JOB_SEED, lengths, start, stop)
+
+
+def generate_reads(generator, lengths, start, stop, workers):
+    """Reads [start, stop) of the job, generated by `workers` host processes (spawned: this runs
+    before the first CUDA call of the process, and forked children of a CUDA process can hang)."""
+    if workers <= 1 or stop - start < 64:
+        return _gen_part((generator, lengths, start, stop))
+    import concurrent.futures
+    import multiprocessing
+    step = max(16, (stop - start) // (4 * workers))
+    parts = [(generator, lengths, a, min(stop, a + step)) for a in range(start, stop, step)]
+    with concurrent.futures.ProcessPoolExecutor(workers, mp_context=multiprocessing.get_context("spawn")) as ex:
+        out = []
+        for r in ex.map(_gen_part, parts):
+            out += r
+    return out
+
+
+def sub_batches(lengths, limit):
+    """Contiguous read ranges [a, b) of a rank's reads holding at most `limit` samples each (at
+    least one read each)."""
+    out, a, acc = [], 0, 0
+    for i, n in enumerate(lengths):
+        if i > a and acc + int(n) > limit:
+            out.append((a, i))
+            a, acc = i, 0
+        acc += int(n)
+    if len(lengths):
+        out.append((a, len(lengths)))
+    return out
 
 
 def chunk_offsets(tok_off, chunk_len):
@@ -255,14 +312,15 @@ def cpu_round_trip(reads, chunk_len, steps=1, warmup=1, lsb=0, model="lossless")
 
 
 def parity_vs_oracle(pl, reads, n_reads, chunk_len, lsb, model):
-    """Compare the GPU streams of the first `n_reads` reads of the batch (the chunks the last
-    timed compress wrote) with the oracle's streams for the same reads: the oracle's split
+    """Compare the GPU streams of the first `n_reads` reads of the rank's first sub-batch
+    (compressed again after the timed region) with the oracle's streams for the same reads: the oracle's split
     (main.py:504-521) and its compress_chunks with the int_mm MLP (cpu_compression.py:178-257),
     both pinned to the reference's outputs by the golden tests."""
     from oracle import signal
     from oracle.oracle import OracleModel
     from sigcomp_b200.model import load_model
-    n = min(n_reads, len(reads))
+    n = min(n_reads, len(reads), pl.subs[0][1] - pl.subs[0][0])
+    pl.compress(0)                       # the first sub-batch holds the first reads
     tok_off = pl.tok_off[:n + 1].cpu().numpy()
     ntok = np.diff(tok_off)
     k = int(((ntok + chunk_len - 1) // chunk_len).sum())
@@ -288,13 +346,14 @@ def run_reference(args):
     if rank != 0:
         return 0
     n_reads = args.cpu_reads
-    reads, _, _ = make_reads(0, n_reads, args.generator)
+    lengths, _ = job_plan(args.generator, n_reads, "strong", 1)
+    reads = generate_reads(args.generator, lengths, 0, n_reads, 1)
     r = cpu_round_trip(reads, args.chunk_len, steps=args.steps, warmup=args.warmup, lsb=args.lsb, model=args.model)
-    sample = f"{n_reads} reads ({r['samples']} samples) of the {args.workload} generator per step"
+    sample = f"the first {n_reads} reads ({r['samples']} samples) of the {args.workload} job per step"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(r["value"], 4), "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(r["seconds_per_step"] * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": round(r["seconds_per_step"] * 1e3, 1), "higher_is_better": True, "scaling": args.scaling,
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "config": {"workload": f"{args.workload_desc}, chunk_len {args.chunk_len}", "reads_per_step": n_reads,
                    "samples_per_step": r["samples"]},
@@ -308,28 +367,43 @@ def run_reference(args):
 
 
 class Pipeline:
-    """Device buffers and the C-ABI calls of one rank's round trip."""
+    """Device buffers and the C-ABI calls of one rank's round trips.  The rank's reads (x) and
+    the decoded reads (y) stay resident; the split, token, stream and offset buffers are sized
+    for the largest sub-batch and reused by every sub-batch."""
 
-    def __init__(self, codec, n_reads, n_samples, chunk_len, lsb=0):
+    def __init__(self, codec, read_lengths, subs, chunk_len, lsb=0):
         import ctypes
         import torch
         self.torch, self.vp = torch, ctypes.c_void_p
         self.L, self.h = codec._lib, codec.handle
         self.chunk_len, self.lsb = chunk_len, lsb
-        self.R, self.S = n_reads, n_samples
         dev = torch.device("cuda", torch.cuda.current_device())
-        cap = max(n_samples - n_reads, 1)
+        lengths = np.asarray(read_lengths, dtype=np.int64)
+        self.soff_h = np.zeros(len(lengths) + 1, np.int64)
+        np.cumsum(lengths, out=self.soff_h[1:])
+        self.S = int(self.soff_h[-1])
+        self.subs = subs
+        # every sub-batch's sample offsets relative to its first sample, back to back
+        rel, self.rel_at = [], []
+        for a, b in subs:
+            self.rel_at.append(sum(len(r) for r in rel))
+            rel.append(self.soff_h[a:b + 1] - self.soff_h[a])
+        self.soff_rel_h = np.concatenate(rel) if rel else np.zeros(1, np.int64)
+        max_reads = max((b - a for a, b in subs), default=1)
+        max_samples = max((int(self.soff_h[b] - self.soff_h[a]) for a, b in subs), default=1)
+        cap = max(max_samples - 1, 1)
 
         def e(n, dt):
-            return torch.empty(n, dtype=dt, device=dev)
+            return torch.empty(max(int(n), 1), dtype=dt, device=dev)
 
-        self.x, self.y = e(n_samples, torch.int16), e(n_samples, torch.int16)
-        self.soff = e(n_reads + 1, torch.int64)
-        self.sig0 = e(n_reads, torch.int16)
+        self.x, self.y = e(self.S, torch.int16), e(self.S, torch.int16)
+        self.soff_rel = e(len(self.soff_rel_h), torch.int64)
+        self.soff_rel.copy_(torch.from_numpy(self.soff_rel_h))
+        self.sig0 = e(max_reads, torch.int16)
         self.tok, self.tok2 = e(cap, torch.uint8), e(cap, torch.uint8)
-        self.tok_off, self.large_off = e(n_reads + 1, torch.int64), e(n_reads + 1, torch.int64)
+        self.tok_off, self.large_off = e(max_reads + 1, torch.int64), e(max_reads + 1, torch.int64)
         self.large, self.pos = e(cap, torch.int16), e(cap, torch.int32)
-        max_chunks = cap // chunk_len + n_reads + 1          # every read adds at most one partial chunk
+        max_chunks = cap // chunk_len + max_reads + 1        # every read adds at most one partial chunk
         self.word_cap = cap + 2 * max_chunks + 1
         self.words = e(self.word_cap, torch.int32)
         self.choff = e(max_chunks + 1, torch.int64)
@@ -338,17 +412,26 @@ class Pipeline:
         self.stream = torch.cuda.current_stream()
         self.n_chunks = 0
         self.chlen_h = np.zeros(0, np.int64)
+        self.cur = None
 
-    def p(self, t):
-        return self.vp(t.data_ptr())
+    def p(self, t, elem_offset=0):
+        return self.vp(t.data_ptr() + elem_offset * t.element_size())
 
-    def compress(self):
+    def sub(self, i):
+        """(reads, first sample, samples, offset of its relative sample offsets) of sub-batch i."""
+        a, b = self.subs[i]
+        return b - a, int(self.soff_h[a]), int(self.soff_h[b] - self.soff_h[a]), self.rel_at[i]
+
+    def compress(self, i):
         from sigcomp_b200 import _lib
         L, h, p, sp = self.L, self.h, self.p, self.vp(self.stream.cuda_stream)
-        _lib.check(L.sc_split_signal_device(h, p(self.x), p(self.soff), self.R, self.lsb, p(self.sig0), p(self.tok),
-                                            p(self.tok_off), p(self.large), p(self.pos), p(self.large_off), sp))
+        R, s0, _, ro = self.sub(i)
+        self.cur = i
+        _lib.check(L.sc_split_signal_device(h, p(self.x, s0), p(self.soff_rel, ro), R, self.lsb, p(self.sig0),
+                                            p(self.tok), p(self.tok_off), p(self.large), p(self.pos),
+                                            p(self.large_off), sp))
         # chunk boundaries of the per-read token streams (host, from the R + 1 token offsets)
-        choff = chunk_offsets(self.tok_off.cpu().numpy(), self.chunk_len)
+        choff = chunk_offsets(self.tok_off[:R + 1].cpu().numpy(), self.chunk_len)
         n = len(choff) - 1
         self.n_chunks = n
         self.chlen_h = np.ascontiguousarray(np.diff(choff), dtype=np.int64)
@@ -357,15 +440,22 @@ class Pipeline:
         _lib.check(L.sc_compress_chunks_device(h, p(self.tok), p(self.choff), n, p(self.words), self.word_cap,
                                                p(self.woff), None, sp))
 
-    def decompress(self):
+    def decompress(self, i):
         from sigcomp_b200 import _lib
         L, h, p, sp = self.L, self.h, self.p, self.vp(self.stream.cuda_stream)
+        R, s0, _, ro = self.sub(i)
         _lib.check(L.sc_decompress_chunks_device(h, p(self.words), p(self.woff), p(self.chlen),
                                                  self.vp(self.chlen_h.ctypes.data), self.n_chunks, p(self.tok2),
                                                  None, sp))
-        _lib.check(L.sc_reassemble_signal_device(h, p(self.sig0), p(self.soff), self.R, self.lsb, p(self.tok2),
+        _lib.check(L.sc_reassemble_signal_device(h, p(self.sig0), p(self.soff_rel, ro), R, self.lsb, p(self.tok2),
                                                  p(self.tok_off), p(self.large), p(self.pos), p(self.large_off),
-                                                 p(self.y), sp))
+                                                 p(self.y, s0), sp))
+
+    def counts(self):
+        """(tokens, large deltas, chunks, words) of the sub-batch last compressed."""
+        R = self.sub(self.cur)[0]
+        return (int(self.tok_off[R].item()), int(self.large_off[R].item()), self.n_chunks,
+                int(self.woff[self.n_chunks].item()))
 
 
 def main():
@@ -373,37 +463,62 @@ def main():
     if args.impl == "reference":
         return run_reference(args)
 
-    import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-    from sigcomp_b200 import _lib
-    from sigcomp_b200.codec import B200Compression
-    from sigcomp_b200.model import load_model
-
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    # this rank's reads, generated before the first CUDA call (by spawned helper processes)
+    lengths, plans = job_plan(args.generator, args.reads, args.scaling, world)
+    plan = plans[rank]
+    workers = args.gen_workers or max(1, min(16, (os.cpu_count() or 1) // max(world, 1)))
+    reads = generate_reads(args.generator, lengths, plan.start, plan.stop, workers)
+    samples_np = np.concatenate(reads) if reads else np.zeros(0, np.int16)
+    n_reads, n_samples = len(reads), len(samples_np)
+    subs = sub_batches(lengths[plan.start:plan.stop], args.sub_samples)
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    from sigcomp_b200 import _lib, sharding
+    from sigcomp_b200.codec import B200Compression
+    from sigcomp_b200.model import load_model
+
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
-    reads, samples_np, soff_np = make_reads(rank, args.reads, args.generator)
-    n_reads, n_samples = len(reads), int(soff_np[-1])
     codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name=args.model))
-    pl = Pipeline(codec, n_reads, n_samples, args.chunk_len, args.lsb)
-    want = torch.from_numpy(lossy_round_trip(samples_np, args.lsb)).cuda()   # what the round trip must return
-    pl.x.copy_(torch.from_numpy(samples_np))
-    pl.soff.copy_(torch.from_numpy(soff_np))
-    counts = torch.zeros(world, dtype=torch.int64, device="cuda")
+    pl = Pipeline(codec, lengths[plan.start:plan.stop], subs, args.chunk_len, args.lsb)
+    pl.x[:n_samples].copy_(torch.from_numpy(samples_np))
+    # what the round trip must return: the reads themselves, or SigComp's lossy output
+    want = pl.x if args.lsb == 0 else torch.from_numpy(lossy_round_trip(samples_np, args.lsb)).cuda()
+    state = {"bytes": 0, "tokens": 0, "large": 0, "chunks": 0}
 
     def exchange():
-        if world > 1:   # archive layout: every rank learns every shard's stream size
-            dist.all_gather_into_tensor(counts, pl.woff[pl.n_chunks:pl.n_chunks + 1].contiguous())
+        # archive layout: every rank learns every shard's stream size (one int64 per rank)
+        return sharding.exchange_shard_bytes(state["bytes"], device=torch.device("cuda", local)) \
+            if world > 1 else [state["bytes"]]
 
-    def step():
-        pl.compress()
-        exchange()
-        pl.decompress()
+    def step(timers=None):
+        state.update(bytes=0, tokens=0, large=0, chunks=0)
+        for i in range(len(subs)):
+            if timers:
+                timers[0].append(torch.cuda.Event(enable_timing=True))
+                timers[0][-1].record()
+            pl.compress(i)
+            tok, large, chunks, words = pl.counts()
+            # bits: framed neural streams (2-byte frame per chunk + words)
+            state["bytes"] += 4 * words + 2 * chunks
+            state["tokens"] += tok
+            state["large"] += large
+            state["chunks"] += chunks
+            if timers:
+                timers[1].append(torch.cuda.Event(enable_timing=True))
+                timers[1][-1].record()
+            pl.decompress(i)
+            if timers:
+                timers[2].append(torch.cuda.Event(enable_timing=True))
+                timers[2][-1].record()
+        return exchange()
 
     def sync():
         torch.cuda.synchronize()
@@ -413,13 +528,8 @@ def main():
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    ok = bool(torch.equal(pl.y, want))
-    n_tok = int(pl.tok_off[-1].item())
-    n_large = int(pl.large_off[-1].item())
-    n_chunks = pl.n_chunks
-    n_words = int(pl.woff[n_chunks].item())
-    # bits: framed neural streams (2-byte frame per chunk + words) over the samples
-    stream_bytes = 4 * n_words + 2 * n_chunks
+    ok = bool(torch.equal(pl.y[:n_samples], want[:n_samples]))
+    n_tok, n_large, n_chunks, stream_bytes = state["tokens"], state["large"], state["chunks"], state["bytes"]
 
     # timed region (device-resident), with per-phase events and per-kernel profiling
     _lib.profile_enable(codec.handle, True)
@@ -429,26 +539,20 @@ def main():
     sync()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     ev[0].record()
-    t_comp = t_dec = 0.0
+    timers = ([], [], [])
+    shard_bytes = None
     for _ in range(args.steps):
-        a, b, c = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-        a.record()
-        pl.compress()
-        exchange()
-        b.record()
-        pl.decompress()
-        c.record()
-        torch.cuda.synchronize()
-        t_comp += a.elapsed_time(b)
-        t_dec += b.elapsed_time(c)
+        shard_bytes = step(timers)
     ev[1].record()
     sync()
     clk = clocks.stop()
     elapsed_ms = ev[0].elapsed_time(ev[1])
+    t_comp = sum(a.elapsed_time(b) for a, b in zip(timers[0], timers[1]))
+    t_dec = sum(b.elapsed_time(c) for b, c in zip(timers[1], timers[2]))
     launches = _lib.kernel_launches() - launches0
     prof = _lib.profile_read(codec.handle)
     _lib.profile_enable(codec.handle, False)
-    ok = ok and bool(torch.equal(pl.y, want))
+    ok = ok and bool(torch.equal(pl.y[:n_samples], want[:n_samples]))
 
     def max_over_ranks(x):
         if world == 1:
@@ -465,6 +569,7 @@ def main():
         return float(t.item())
 
     elapsed_max = max_over_ranks(elapsed_ms)
+    elapsed_min = -max_over_ranks(-elapsed_ms)
     t_comp_max = max_over_ranks(t_comp)
     t_dec_max = max_over_ranks(t_dec)
     total_samples = sum_over_ranks(n_samples)
@@ -472,47 +577,49 @@ def main():
     total_tokens = sum_over_ranks(n_tok)
     total_large = sum_over_ranks(n_large)
     all_ok = sum_over_ranks(0.0 if ok else 1.0) == 0
+    layout_ok = shard_bytes is not None and int(sum(shard_bytes)) == int(total_stream)
 
     # ---- e2e: reads from pinned host memory, record streams out and back, reads out ------
     e2e = None
     if not args.no_e2e:
         def pinned(n, dt):
-            return torch.empty(n, dtype=dt).pin_memory()
+            return torch.empty(max(int(n), 1), dtype=dt).pin_memory()
 
-        # host buffers sized to this batch's record streams (the same every step), not to the
-        # device-side upper bounds: a rank pins about 2 x 2 B per sample plus the streams
-        h_x = torch.from_numpy(samples_np).pin_memory()
-        h_soff = torch.from_numpy(soff_np).pin_memory()
+        # host buffers: the rank's reads in and out, and one sub-batch's record streams
+        h_x = torch.from_numpy(samples_np).pin_memory() if n_samples else pinned(1, torch.int16)
+        h_soff = torch.from_numpy(pl.soff_rel_h).pin_memory()
         h_y = pinned(n_samples, torch.int16)
-        h_words, h_woff = pinned(n_words + 1, torch.int32), pinned(n_chunks + 1, torch.int64)
-        h_large, h_pos = pinned(max(n_large, 1), torch.int16), pinned(max(n_large, 1), torch.int32)
-        h_sig0 = pinned(n_reads, torch.int16)
-        h_tokoff, h_loff = pinned(n_reads + 1, torch.int64), pinned(n_reads + 1, torch.int64)
+        cap = pl.word_cap
+        h_words, h_woff = pinned(cap, torch.int32), pinned(pl.woff.numel(), torch.int64)
+        h_large, h_pos = pinned(pl.large.numel(), torch.int16), pinned(pl.pos.numel(), torch.int32)
+        h_sig0 = pinned(pl.sig0.numel(), torch.int16)
+        h_tokoff, h_loff = pinned(pl.tok_off.numel(), torch.int64), pinned(pl.large_off.numel(), torch.int64)
         moved = {"h2d": 0, "d2h": 0}
 
-        def copy(dst, src, n, kind):
-            n = src.numel() if n is None else n
-            dst[:n].copy_(src[:n], non_blocking=True)
+        def copy(dst, src, n, kind, dst_at=0, src_at=0):
+            dst[dst_at:dst_at + n].copy_(src[src_at:src_at + n], non_blocking=True)
             moved[kind] += n * src.element_size()
 
         def host_step():
-            copy(pl.x, h_x, None, "h2d")
-            copy(pl.soff, h_soff, None, "h2d")
-            pl.compress()
+            copy(pl.soff_rel, h_soff, h_soff.numel(), "h2d")
+            for i in range(len(subs)):
+                R, s0, ns, _ = pl.sub(i)
+                copy(pl.x, h_x, ns, "h2d", s0, s0)
+                pl.compress(i)
+                _, nl, nc, nw = pl.counts()
+                # the record streams of the archive: words + offsets, large values, positions, sig0, offsets
+                streams = ((h_words, pl.words, nw), (h_woff, pl.woff, nc + 1), (h_large, pl.large, nl),
+                           (h_pos, pl.pos, nl), (h_sig0, pl.sig0, R), (h_tokoff, pl.tok_off, R + 1),
+                           (h_loff, pl.large_off, R + 1))
+                for hb, db, n in streams:
+                    copy(hb, db, n, "d2h")
+                torch.cuda.current_stream().synchronize()
+                for hb, db, n in streams:
+                    copy(db, hb, n, "h2d")
+                pl.decompress(i)
+                copy(h_y, pl.y, ns, "d2h", s0, s0)
+            torch.cuda.current_stream().synchronize()
             exchange()
-            nw, nl, nc = int(pl.woff[pl.n_chunks].item()), int(pl.large_off[-1].item()), pl.n_chunks
-            # the record streams of the archive: words + offsets, large values, positions, sig0, offsets
-            streams = ((h_words, pl.words, nw), (h_woff, pl.woff, nc + 1), (h_large, pl.large, nl),
-                       (h_pos, pl.pos, nl), (h_sig0, pl.sig0, None), (h_tokoff, pl.tok_off, None),
-                       (h_loff, pl.large_off, None))
-            for hb, db, n in streams:
-                copy(hb, db, n, "d2h")
-            torch.cuda.current_stream().synchronize()
-            for hb, db, n in streams:
-                copy(db, hb, n, "h2d")
-            pl.decompress()
-            copy(h_y, pl.y, None, "d2h")
-            torch.cuda.current_stream().synchronize()
 
         host_step()
         sync()
@@ -524,7 +631,7 @@ def main():
         e1.record()
         sync()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-        ok_e2e = bool(np.array_equal(h_y.numpy(), want.cpu().numpy()))
+        ok_e2e = bool(np.array_equal(h_y.numpy()[:n_samples], want[:n_samples].cpu().numpy()))
         all_ok = all_ok and sum_over_ranks(0.0 if ok_e2e else 1.0) == 0
         e2e = {"value": round(total_samples * args.steps / (e2e_ms * 1e-3) / 1e6, 3), "unit": UNIT,
                "h2d_bytes_per_step": int(moved["h2d"] // args.steps),
@@ -572,23 +679,29 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         if args.parity_reads > 0:
             parity = parity_vs_oracle(pl, reads, args.parity_reads, args.chunk_len, args.lsb, args.model)
-        n = min(args.cpu_reads, args.reads)
+        n = min(args.cpu_reads, len(reads))
         r = cpu_round_trip(reads[:n], args.chunk_len, steps=1, warmup=1, lsb=args.lsb, model=args.model)
         cpu = {"value": round(r["value"], 4), "unit": UNIT, "cores": r["cores"], "kind": "port",
-               "sample": f"first {n} reads of the same batch ({r['samples']} samples), one round trip after one "
+               "sample": f"first {n} reads of the same job ({r['samples']} samples), one round trip after one "
                          "warm-up",
                "compress_msps": round(r["compress"], 4), "decompress_msps": round(r["decompress"], 4)}
 
     if rank == 0:
         value = total_samples * args.steps / (elapsed_max * 1e-3) / 1e6
+        job_reads = args.reads * world if args.scaling == "weak" else args.reads
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps, 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "scaling": args.scaling, "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": f"{args.workload_desc}, chunk_len {args.chunk_len}",
-                       "reads_per_gpu": args.reads, "samples_per_gpu": n_samples, "tokens_per_gpu": n_tok,
-                       "chunks_per_gpu": n_chunks, "parallelism": f"reads sharded over {world} GPU(s)",
-                       "step": "split -> compress -> decompress -> reassemble, int16 reads in and out",
+                       "job_reads": job_reads, "job_samples": int(total_samples),
+                       "reads_per_gpu": n_reads, "samples_per_gpu": n_samples, "tokens_per_gpu": n_tok,
+                       "chunks_per_gpu": n_chunks, "sub_batches_per_gpu": len(subs),
+                       "parallelism": f"reads sharded over {world} GPU(s) by sample count "
+                                      "(sharding.sample_balanced_ranges); shard byte counts all-gathered once per "
+                                      "step (sharding.exchange_shard_bytes)",
+                       "step": "split -> compress -> decompress -> reassemble of every sub-batch, int16 reads in "
+                               "and out",
                        "l2": (f"inputs larger than L2 ({2 * n_samples / 1e9:.2f} GB of samples, "
                               f"{n_tok / 1e9:.2f} GB of tokens per GPU); no flush needed"
                               if 2 * n_samples > L2_BYTES else
@@ -596,10 +709,12 @@ def main():
                               "not flushed between steps")},
             "compress_msps": round(total_samples * args.steps / (t_comp_max * 1e-3) / 1e6, 3),
             "decompress_msps": round(total_samples * args.steps / (t_dec_max * 1e-3) / 1e6, 3),
+            "rank_balance": round(elapsed_min / elapsed_max, 4) if elapsed_max else None,
             "bits_per_sample_neural": round(8 * total_stream / total_samples, 4),
             "bits_per_small_token": round(8 * total_stream / total_tokens, 4),
             "large_delta_fraction": round(total_large / max(total_samples, 1), 5),
             "bit_exact_round_trip": all_ok,
+            "archive_layout_consistent": layout_ok,
             "parity_vs_oracle": parity,
             "gpu_launches": int(launches),
             "clocks": clk, "roofline": roofline, "roofline_compress": roofline_c, "cpu_baseline": cpu,

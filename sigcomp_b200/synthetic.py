@@ -12,6 +12,11 @@ distributions follow the benchmark configurations of the SigComp evaluation:
   [2,000, 1,000,000]) with the same level/dwell/noise parameters.
 * ``rna_lognormal``: levels N(800, 90), dwell 30, noise 20, lognormal lengths
   (median 15,000, sigma_log 0.9).
+* ``r10_lognormal_large``: configuration 5's 200,000 reads, lognormal lengths (median
+  40,000, sigma_log 0.8), R10 levels.
+
+``job_lengths`` / ``job_reads`` draw the same distributions for the sharded benchmark jobs,
+with one generator per read so that every rank makes only its own reads.
 """
 
 from dataclasses import dataclass
@@ -57,6 +62,33 @@ def synth_read(rng, n, model=R10):
 def lognormal_lengths(rng, count, median, sigma_log, lo=2000, hi=1_000_000):
     lengths = rng.lognormal(np.log(median), sigma_log, size=int(count))
     return np.clip(np.rint(lengths), lo, hi).astype(np.int64)
+
+
+# Read sets of the sharded benchmark jobs: lengths drawn first from one generator (cheap for
+# any count), samples of read i from their own generator seeded by (seed, i), so that a rank
+# can make exactly its share of a job without the reads before it.
+JOB_SETS = {
+    "r10_config1": (64, None, R10),
+    "r10_lognormal": (20000, (30000, 0.8), R10),
+    "r10_lognormal_large": (200000, (40000, 0.8), R10),      # configuration 5: ~8 G samples
+    "rna_lognormal": (10000, (15000, 0.9), RNA004),
+}
+
+
+def job_lengths(config, seed, count):
+    """Sample counts of the first ``count`` reads of a sharded job (``count`` may exceed the
+    configuration's read count: the lengths continue from the same distribution)."""
+    base, dist, _ = JOB_SETS[config]
+    if dist is None:
+        return np.full(int(count), 20000, dtype=np.int64)
+    rng = np.random.default_rng(seed)
+    return lognormal_lengths(rng, int(count), dist[0], dist[1])
+
+
+def job_reads(config, seed, lengths, start, stop):
+    """Reads ``[start, stop)`` of a sharded job whose read lengths are ``lengths``."""
+    model = JOB_SETS[config][2]
+    return [synth_read(np.random.default_rng([int(seed), i]), lengths[i], model) for i in range(start, stop)]
 
 
 def make_reads(config, seed=0, count=None):

@@ -30,9 +30,44 @@ def test_chunk_offsets_empty():
 
 
 def test_workloads_cover_baseline_configurations():
-    assert set(bench.WORKLOADS) == {"config1", "config2", "config3", "config4"}
+    assert set(bench.WORKLOADS) == {"config1", "config2", "config3", "config4", "config5"}
     assert bench.WORKLOADS["config2"][:4] == ("r10_lognormal", 20000, "lossless", 0)
+    assert bench.WORKLOADS["config2"][5] == "weak"
     assert bench.WORKLOADS["config4"][2:4] == ("lossy", 3)
+    assert bench.WORKLOADS["config5"][:2] == ("r10_lognormal_large", 200000)
+    assert bench.WORKLOADS["config5"][5] == "strong"
+
+
+def test_job_plan_shards_one_job_by_sample_count():
+    from sigcomp_b200 import sharding
+    # weak: the job grows with the ranks, each rank's range balanced by sample count
+    lengths, plans = bench.job_plan("r10_lognormal", 1000, "weak", 4)
+    assert len(lengths) == 4000 and len(plans) == 4
+    assert plans[0].start == 0 and plans[-1].stop == 4000
+    assert all(a.stop == b.start for a, b in zip(plans, plans[1:]))
+    assert tuple(plans) == sharding.sample_balanced_ranges(lengths, 4)
+    share = [p.num_samples / lengths.sum() for p in plans]
+    assert max(share) - min(share) < 0.01
+    # strong: one job of fixed size over every rank count; a prefix of the configuration-5 lengths
+    l1, p1 = bench.job_plan("r10_lognormal_large", 5000, "strong", 1)
+    l8, p8 = bench.job_plan("r10_lognormal_large", 5000, "strong", 8)
+    assert np.array_equal(l1, l8) and len(p8) == 8 and p1[0].num_samples == sum(p.num_samples for p in p8)
+
+
+def test_sub_batches_bound_the_samples():
+    lengths = np.array([5, 5, 5, 20, 1, 1, 30, 2], np.int64)
+    subs = bench.sub_batches(lengths, 12)
+    assert subs == [(0, 2), (2, 3), (3, 4), (4, 6), (6, 7), (7, 8)]
+    assert bench.sub_batches(lengths, 10 ** 9) == [(0, 8)]
+    assert bench.sub_batches(np.zeros(0, np.int64), 10) == []
+
+
+def test_generated_reads_do_not_depend_on_the_workers():
+    lengths, _ = bench.job_plan("r10_lognormal", 80, "strong", 1)
+    a = bench.generate_reads("r10_lognormal", lengths, 10, 80, 1)
+    b = bench.generate_reads("r10_lognormal", lengths, 10, 80, 2)
+    assert len(a) == 70 and all(np.array_equal(x, y) for x, y in zip(a, b))
+    assert [len(x) for x in a] == lengths[10:80].tolist()
 
 
 def test_lossy_round_trip_matches_signal_module():
