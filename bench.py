@@ -104,6 +104,8 @@ def parse_args():
                          "only, int_mm MLP: a few seconds of CPU work per 100 reads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-plugin", action="store_true",
+                    help="skip e2e_plugin (the read-level codec interface with host bytes in and out)")
     ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
                     help="tokens per chunk (2048 in every configuration; smaller values give short "
                          "decoder launches for profiling)")
@@ -640,6 +642,48 @@ def main():
                                "sc_decompress_chunks_device + sc_reassemble_signal_device; every step's reads "
                                "and record streams through pinned host memory"}
 
+    # ---- e2e_plugin: SigComp's own integration route, GPUCompression.batch_inference_reads with
+    # host token streams in and framed host bytes out, then the framed bytes back to tokens
+    # (cpu_compression.py:28-84; callers main.py:873, 1150), one call per sub-batch as SigComp's
+    # flush loops call it per batch.  The token streams come from the split of the same reads
+    # (the caller's _split_signal), made before the timed region.
+    e2e_plugin = None
+    if not args.no_plugin:
+        toks = []
+        for i in range(len(subs)):
+            a_, b_ = subs[i]
+            toks.append([sp[1] for sp in codec.split_signals(reads[a_:b_], lsb=args.lsb)])
+        samples_sub = [int(pl.soff_h[b_] - pl.soff_h[a_]) for a_, b_ in subs]
+
+        def plugin_step():
+            out, nbytes = [], 0
+            for t in toks:
+                framed = codec.batch_inference_reads(list_of_reads=t, batch_size=20480)
+                nbytes += sum(len(f) for f in framed)
+                out.append(codec.batch_inference_reads(list_of_compressed_reads=framed,
+                                                       list_of_lengths=[len(x) for x in t], batch_size=20480))
+            return out, nbytes
+
+        plugin_step()                       # warm-up: the model's buffers grow to this batch
+        sync()
+        t0 = time.perf_counter()
+        p_back, p_bytes = plugin_step()
+        torch.cuda.synchronize()
+        p_s = max_over_ranks(time.perf_counter() - t0)
+        p_ok = all(np.array_equal(x, y) for bt, t in zip(p_back, toks) for x, y in zip(bt, t))
+        del p_back
+        all_ok = all_ok and sum_over_ranks(0.0 if p_ok else 1.0) == 0
+        tok_bytes = sum(sum(len(x) for x in t) for t in toks)
+        e2e_plugin = {
+            "value": round(total_samples / p_s / 1e6, 3), "unit": UNIT, "steps": 1,
+            "seconds_per_step": round(p_s, 3), "frac_of_value": None,
+            "host_bytes_in_per_step": int(sum_over_ranks(tok_bytes + p_bytes)),
+            "host_bytes_out_per_step": int(sum_over_ranks(p_bytes + tok_bytes)),
+            "route": "GPUCompression.batch_inference_reads(list_of_reads=...) then "
+                     "(list_of_compressed_reads=..., list_of_lengths=...), host numpy tokens in, framed bytes "
+                     "out and back, one call pair per sub-batch; wall clock, max over ranks (host work included)",
+        }
+
     # ---- roofline of the fused kernels ------------------------------------------
     roofline = roofline_c = None
     if rank == 0:
@@ -719,7 +763,10 @@ def main():
             "gpu_launches": int(launches),
             "clocks": clk, "roofline": roofline, "roofline_compress": roofline_c, "cpu_baseline": cpu,
             "e2e": e2e,
+            "e2e_plugin": e2e_plugin,
         }
+        if e2e_plugin is not None:
+            e2e_plugin["frac_of_value"] = round(e2e_plugin["value"] / value, 4)
         print(json.dumps(line), flush=True)
     codec.close()
     if world > 1:

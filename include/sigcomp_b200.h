@@ -166,6 +166,37 @@ SC_API int sc_decode_logits_device(sc_model *model, const int8_t *logits, const 
                                    uint8_t *symbols, uint8_t *stream_errors, void *stream);
 
 /*
+ * SIG2 read framing on the host (no device work), for the read-level interface
+ * ReadFramingMixin.batch_inference_reads (sigcomp/cpu_compression.py:28-84): a
+ * compressed read is its chunks' streams in order, each preceded by its byte
+ * count as a little-endian uint16.
+ *
+ * sc_frame_reads: read r holds chunks read_chunks[r] .. read_chunks[r+1] of the
+ * streams in `words` / `word_offsets` (as written by sc_compress_chunks); its
+ * framed bytes go to out[out_offsets[r] .. out_offsets[r+1]) (out_offsets has
+ * n_reads + 1 entries).  A stream above 65535 bytes returns
+ * SC_ERR_INVALID_ARGUMENT with the reference's message; too small an
+ * out_capacity returns SC_ERR_CAPACITY.
+ */
+SC_API int sc_frame_reads(const uint32_t *words, const int64_t *word_offsets, const int64_t *read_chunks,
+                          int64_t n_reads, uint8_t *out, int64_t out_capacity, int64_t *out_offsets);
+
+/*
+ * sc_unframe_reads: the inverse, with the reference's checks and messages in
+ * read order.  Read r is reads[r][0 .. read_bytes[r]) holding token_lengths[r]
+ * tokens in chunks of chunk_len; its streams are appended to `words` (chunk c =
+ * words[word_offsets[c] .. word_offsets[c+1]), chunk_lengths[c] tokens) and its
+ * chunks are read_chunks[r] .. read_chunks[r+1].  On a malformed read, returns
+ * SC_ERR_INVALID_ARGUMENT ("Truncated SIG2 chunk length", "Invalid or truncated
+ * SIG2 range-coded chunk", "Trailing SIG2 chunk data disagrees with token
+ * length", "Token lengths must be nonnegative integers") with *bad_read = r.
+ */
+SC_API int sc_unframe_reads(const uint8_t *const *reads, const int64_t *read_bytes, const int64_t *token_lengths,
+                            int64_t n_reads, int32_t chunk_len, uint32_t *words, int64_t words_capacity,
+                            int64_t *word_offsets, int64_t *chunk_lengths, int64_t chunks_capacity,
+                            int64_t *read_chunks, int64_t *bad_read);
+
+/*
  * SigComp's signal split on the device: _split_signal (sigcomp/main.py:504-521)
  * of every read, after the lossy step _lossy_encode(_reduce_lsb(read, lsb), lsb)
  * (main.py:158-171) when lsb > 0.  Every array is in device memory.

@@ -8,7 +8,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libsigcomp_b200.so"
-SOURCES = ["sc_capi.cu", "sc_codec.cu", "sc_mlp_simple.cu", "sc_mlp_tc.cu", "sc_signal.cu"]
+SOURCES = ["sc_capi.cu", "sc_codec.cu", "sc_frames.cu", "sc_mlp_simple.cu", "sc_mlp_tc.cu", "sc_signal.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a", "-lineinfo", "-O3", "-std=c++17",

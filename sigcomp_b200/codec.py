@@ -285,55 +285,55 @@ class B200Compression:
                 offsets[:-1] = starts
                 offsets[-1] = ends[-1]
             words, woff = self.compress_flat(tokens, offsets) if n else (np.zeros(0, np.uint32), offsets[:1])
-            nbytes = 4 * np.diff(woff)
-            if np.any(nbytes > 65535):
-                raise ValueError("Compressed chunk exceeds the SIG2 uint16 frame; compress with a smaller --chunk-len")
-            raw = words.astype("<u4", copy=False).view(np.uint8)
-            result = []
-            for r in range(len(reads)):
-                c0, c1 = int(first_chunk[r]), int(first_chunk[r + 1])
-                framed = bytearray()
-                for c in range(c0, c1):
-                    framed += _CHUNK_LENGTH.pack(int(nbytes[c]))
-                    framed += raw[4 * woff[c]:4 * woff[c + 1]].tobytes()
-                result.append(bytes(framed))
-            return result
+            # frames of every read in one pass (sc_frame_reads: the reference's checks, in C)
+            words = np.ascontiguousarray(words, dtype=np.uint32)
+            if not len(words):
+                words = np.zeros(1, np.uint32)
+            cap = 4 * int(woff[-1]) + 2 * n
+            out = np.empty(max(cap, 1), dtype=np.uint8)
+            out_off = np.zeros(len(reads) + 1, dtype=np.int64)
+            first_chunk = np.ascontiguousarray(first_chunk, dtype=np.int64)
+            rc = _lib.load().sc_frame_reads(_ptr(words), _ptr(woff), _ptr(first_chunk), len(reads), _ptr(out), len(out),
+                                          _ptr(out_off))
+            _lib.check(rc, "sc_frame_reads")
+            return [out[out_off[r]:out_off[r + 1]].tobytes() for r in range(len(reads))]
 
         if list_of_compressed_reads is None or list_of_lengths is None:
             raise ValueError("Compressed reads and token lengths are required")
         if len(list_of_compressed_reads) != len(list_of_lengths):
             raise ValueError("Compressed read and token length counts differ")
-        chunks, lengths, mapping = [], [], []
-        for data, length in zip(list_of_compressed_reads, list_of_lengths):
+        # reads are checked in order, as the reference does: the first bad token length stops the
+        # parse there, after the reads before it have been checked
+        n_reads = len(list_of_lengths)
+        good = n_reads
+        for i, length in enumerate(list_of_lengths):
             if int(length) != length or length < 0:
-                raise ValueError("Token lengths must be nonnegative integers")
-            remaining, pos, begin = int(length), 0, len(chunks)
-            while remaining:
-                if pos + _CHUNK_LENGTH.size > len(data):
-                    raise ValueError("Truncated SIG2 chunk length")
-                size, = _CHUNK_LENGTH.unpack_from(data, pos)
-                pos += _CHUNK_LENGTH.size
-                if size == 0 or size % 4 or pos + size > len(data):
-                    raise ValueError("Invalid or truncated SIG2 range-coded chunk")
-                count = min(L, remaining)
-                chunks.append(data[pos:pos + size])
-                lengths.append(count)
-                pos += size
-                remaining -= count
-            if pos != len(data):
-                raise ValueError("Trailing SIG2 chunk data disagrees with token length")
-            mapping.append((begin, len(chunks)))
-        n = len(chunks)
+                good = i
+                break
+        data = [d if isinstance(d, bytes) else bytes(d) for d in list_of_compressed_reads[:good]]
+        lens = np.asarray([int(x) for x in list_of_lengths[:good]], dtype=np.int64)
+        nbytes = np.asarray([len(d) for d in data], dtype=np.int64)
+        chunks_cap = int(((lens + L - 1) // L).sum())
+        words_cap = int(nbytes.sum()) // 4
+        words = np.empty(max(words_cap, 1), dtype=np.uint32)
+        woff = np.zeros(chunks_cap + 1, dtype=np.int64)
+        clen = np.zeros(max(chunks_cap, 1), dtype=np.int64)
+        read_chunks = np.zeros(good + 1, dtype=np.int64)
+        bad = np.full(1, -1, dtype=np.int64)
+        ptrs = (ctypes.c_char_p * max(good, 1))(*data) if good else (ctypes.c_char_p * 1)()
+        rc = _lib.load().sc_unframe_reads(ctypes.cast(ptrs, ctypes.c_void_p), _ptr(nbytes), _ptr(lens), good, L,
+                                        _ptr(words), len(words), _ptr(woff), _ptr(clen), chunks_cap,
+                                        _ptr(read_chunks), _ptr(bad))
+        _lib.check(rc, "sc_unframe_reads")
+        if good < n_reads:
+            raise ValueError("Token lengths must be nonnegative integers")
+        n = int(read_chunks[-1])
         if n == 0:
-            return [np.empty(0, dtype=np.uint8) for _ in mapping]
-        lengths = np.asarray(lengths, dtype=np.int64)
-        woff = np.zeros(n + 1, dtype=np.int64)
-        np.cumsum(np.asarray([len(c) // 4 for c in chunks], dtype=np.int64), out=woff[1:])
-        words = np.frombuffer(b"".join(bytes(c) for c in chunks), dtype="<u4").astype(np.uint32, copy=False)
-        tokens = self.decompress_flat(words, woff, lengths)
-        toff = np.zeros(n + 1, dtype=np.int64)
-        np.cumsum(lengths, out=toff[1:])
-        return [tokens[toff[b]:toff[e]].copy() if e > b else np.empty(0, dtype=np.uint8) for b, e in mapping]
+            return [np.empty(0, dtype=np.uint8) for _ in range(n_reads)]
+        tokens = self.decompress_flat(words[:int(woff[n])], woff[:n + 1], clen[:n])
+        toff = np.zeros(n_reads + 1, dtype=np.int64)
+        np.cumsum(lens, out=toff[1:])
+        return [tokens[toff[r]:toff[r + 1]].copy() for r in range(n_reads)]
 
 
 # The name SigComp's _load_model builds for --device cuda.

@@ -3,6 +3,7 @@ data, framing validation and error mapping."""
 
 import re
 import ctypes
+import struct
 
 import numpy as np
 import pytest
@@ -189,3 +190,66 @@ def test_build_refuses_spills_in_the_fused_kernels():
     ])
     assert spilling_kernels(log) == [("_ZN2sc12_GLOBAL__N_18k_fused2ILb1EEEvNS_12Fused2ParamsE", 36, 44)]
     assert spilling_kernels(log.replace("36 bytes spill stores, 44", "0 bytes spill stores, 0")) == []
+
+
+def test_frame_helpers_round_trip_and_error_order():
+    """sc_frame_reads / sc_unframe_reads (the C passes of batch_inference_reads' framing) on
+    random streams, and the reference's error order: reads are checked one after the other, so
+    the first malformed read decides the message (cpu_compression.py:58-80)."""
+    import ctypes
+    L = _lib.load()
+    rng = np.random.default_rng(12)
+    n_reads, chunk_len = 50, 7
+    lengths = rng.integers(0, 40, size=n_reads)
+    nchunks = (lengths + chunk_len - 1) // chunk_len
+    read_chunks = np.zeros(n_reads + 1, np.int64)
+    np.cumsum(nchunks, out=read_chunks[1:])
+    nwords = rng.integers(1, 20, size=int(read_chunks[-1]))
+    woff = np.zeros(len(nwords) + 1, np.int64)
+    np.cumsum(nwords, out=woff[1:])
+    words = rng.integers(0, 2 ** 32, size=int(woff[-1]), dtype=np.uint64).astype(np.uint32)
+    out = np.empty(4 * len(words) + 2 * len(nwords), np.uint8)
+    out_off = np.zeros(n_reads + 1, np.int64)
+    vp = ctypes.c_void_p
+    assert L.sc_frame_reads(vp(words.ctypes.data), vp(woff.ctypes.data), vp(read_chunks.ctypes.data), n_reads,
+                            vp(out.ctypes.data), len(out), vp(out_off.ctypes.data)) == _lib.SC_OK
+    framed = [out[out_off[r]:out_off[r + 1]].tobytes() for r in range(n_reads)]
+    for r in range(n_reads):           # the reference's frame: '<H' byte count, then the stream
+        want = b"".join(struct.pack("<H", 4 * int(nwords[c])) + words[woff[c]:woff[c + 1]].astype("<u4").tobytes()
+                        for c in range(read_chunks[r], read_chunks[r + 1]))
+        assert framed[r] == want
+
+    def unframe(reads, lens):
+        lens = np.asarray(lens, np.int64)
+        nb = np.asarray([len(d) for d in reads], np.int64)
+        cap_c = int(((np.maximum(lens, 0) + chunk_len - 1) // chunk_len).sum())
+        w = np.empty(max(int(nb.sum()) // 4, 1), np.uint32)
+        wo = np.zeros(cap_c + 1, np.int64)
+        cl = np.zeros(max(cap_c, 1), np.int64)
+        rc_ = np.zeros(len(reads) + 1, np.int64)
+        bad = np.zeros(1, np.int64)
+        ptrs = (ctypes.c_char_p * max(len(reads), 1))(*reads)
+        rc = L.sc_unframe_reads(ctypes.cast(ptrs, vp), vp(nb.ctypes.data), vp(lens.ctypes.data), len(reads),
+                                chunk_len, vp(w.ctypes.data), len(w), vp(wo.ctypes.data), vp(cl.ctypes.data), cap_c,
+                                vp(rc_.ctypes.data), vp(bad.ctypes.data))
+        return rc, int(bad[0]), w, wo, cl, rc_
+
+    rc, bad, w, wo, cl, rc_ = unframe(framed, lengths)
+    assert rc == _lib.SC_OK and bad == -1
+    assert np.array_equal(rc_, read_chunks) and np.array_equal(wo, woff)
+    assert np.array_equal(w[:len(words)], words)
+    assert cl.tolist()[:len(nwords)] == [min(chunk_len, int(lengths[r]) - chunk_len * (c - read_chunks[r]))
+                                         for r in range(n_reads) for c in range(read_chunks[r], read_chunks[r + 1])]
+    # the first malformed read decides: a truncated read 3 before a trailing-data read 7
+    reads = list(framed)
+    k3 = next(r for r in range(3, n_reads) if lengths[r] > 0)
+    k7 = next(r for r in range(k3 + 1, n_reads) if lengths[r] > 0)
+    reads[k3] = reads[k3][:-1]
+    reads[k7] = reads[k7] + b"\x00"
+    rc, bad, *_ = unframe(reads, lengths)
+    assert rc == _lib.SC_ERR_INVALID_ARGUMENT and bad == k3
+    assert b"Invalid or truncated" in L.sc_last_error()
+    reads = list(framed)
+    reads[k7] = reads[k7] + b"\x00"
+    rc, bad, *_ = unframe(reads, lengths)
+    assert bad == k7 and b"Trailing" in L.sc_last_error()
