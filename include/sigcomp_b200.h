@@ -138,6 +138,19 @@ SC_API int sc_mlp_logits_device(sc_model *model, const int16_t *windows, int64_t
                          void *stream);
 
 /*
+ * One integer linear layer of the model alone, on device memory:
+ *   y[rows][out_dims[layer]] = requant(x[rows][in_dims[layer]] * W^T + b)
+ * with the layer's bias, M0/shift and ReLU (cpu_int_kernels.py:5-14), computed by the
+ * tcgen05 layer kernel.  Replaces the reference's per-layer GPU kernel,
+ * bit_exact_linear_kernel (sigcomp/quant_mlp_export.py:21-76), and
+ * CPUBitExactInt8Linear.forward (sigcomp/cpu_int_inference.py:206-256).  For layer 0, x
+ * holds the gathered context windows (x[r][p * emb_dim + c] = E[token_p][c]).  x must be
+ * 16-byte aligned.
+ */
+SC_API int sc_linear_layer_device(sc_model *model, int32_t layer, const int8_t *x, int64_t rows, int8_t *y,
+                                  void *stream);
+
+/*
  * The range coder alone on given int8 logits (no MLP), in device memory.  Replaces the
  * reference's step encoder, GpuRangeStepEncoder (sigcomp/gpu_entropy_coding.py:255-303:
  * encode_step_int8 at every step, then seal and get_compressed), with the byte-exact

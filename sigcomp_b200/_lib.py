@@ -24,7 +24,7 @@ EXPORTS = (
     "sc_decompress_chunks_device", "sc_mlp_logits_device", "sc_profile_enable", "sc_profile_read",
     "sc_trace_enable", "sc_trace_read", "sc_mlp_logits_device_noalloc", "sc_split_signal_device",
     "sc_reassemble_signal_device", "sc_selftest_wait_timeout", "sc_encode_logits_device",
-    "sc_decode_logits_device", "sc_frame_reads", "sc_unframe_reads",
+    "sc_decode_logits_device", "sc_frame_reads", "sc_unframe_reads", "sc_linear_layer_device",
 )
 
 KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step",
@@ -61,6 +61,7 @@ def load():
     L.sc_encode_logits_device.argtypes = [vp, vp, vp, vp, i64, vp, i64, vp, vp, vp]
     L.sc_decode_logits_device.argtypes = [vp, vp, vp, vp, vp, i64, vp, vp, vp]
     L.sc_frame_reads.argtypes = [vp, vp, vp, i64, vp, i64, vp]
+    L.sc_linear_layer_device.argtypes = [vp, i32, vp, i64, vp, vp]
     L.sc_unframe_reads.argtypes = [vp, vp, vp, i64, i32, vp, i64, vp, vp, i64, vp, vp]
     L.sc_profile_enable.argtypes = [vp, i32]
     L.sc_profile_read.argtypes = [vp, i32, vp, vp, vp]
@@ -75,7 +76,7 @@ def load():
                  "sc_mlp_logits_device", "sc_mlp_logits_device_noalloc", "sc_profile_enable",
                  "sc_profile_read", "sc_split_signal_device", "sc_reassemble_signal_device",
                  "sc_selftest_wait_timeout", "sc_encode_logits_device", "sc_decode_logits_device",
-                 "sc_frame_reads", "sc_unframe_reads"):
+                 "sc_frame_reads", "sc_unframe_reads", "sc_linear_layer_device"):
         getattr(L, name).restype = ctypes.c_int
     _lib = L
     return L

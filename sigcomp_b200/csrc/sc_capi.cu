@@ -714,4 +714,27 @@ int sc_decode_logits_device(sc_model *m, const int8_t *logits, const int64_t *of
     });
 }
 
+int sc_linear_layer_device(sc_model *m, int32_t layer, const int8_t *x, int64_t rows, int8_t *y, void *stream)
+{
+    g_err[0] = 0;
+    if (!m || layer < 0 || layer >= m->num_layers || rows < 0 || (rows > 0 && (!x || !y))) {
+        set_error("invalid argument");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    if (!m->tc_ok) {
+        set_error("model geometry not supported by the tcgen05 kernels");
+        return SC_ERR_UNSUPPORTED;
+    }
+    if (((uintptr_t)x & 15) != 0) {
+        set_error("x must be 16-byte aligned");
+        return SC_ERR_INVALID_ARGUMENT;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    return guarded(m, [&]() -> int {
+        linear_tc(m, layer, x, rows, y, s);
+        SC_CUDA(cudaStreamSynchronize(s));
+        return SC_OK;
+    });
+}
+
 }  // extern "C"

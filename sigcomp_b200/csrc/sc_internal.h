@@ -158,6 +158,8 @@ struct L0Source {
 bool mlp_tc_supported(const sc_model *m);
 void mlp_tc(sc_model *m, const L0Source &src, int64_t rows, int64_t l0_tiles, int8_t *logits, cudaStream_t s);
 void mlp_tc_prepare(sc_model *m);
+// One layer alone on explicit int8 activations [rows][in_dim] -> [rows][out_dim].
+void linear_tc(sc_model *m, int layer, const int8_t *x, int64_t rows, int8_t *y, cudaStream_t s);
 
 // Fused persistent kernels (all layers + coder step in one launch).
 bool fused_supported(const sc_model *m);

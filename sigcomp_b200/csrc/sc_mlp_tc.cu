@@ -447,6 +447,25 @@ void mlp_tc(sc_model *m, const L0Source &src, int64_t rows, int64_t l0_tiles, in
     }
 }
 
+// One integer linear layer alone, y = requant(x * W_l^T + b_l), on explicit int8 activations
+// x [rows][in_dim] (layer 0 included: x is then the gathered window rows), with the tcgen05
+// layer kernel: the layer of the reference's bit_exact_linear_kernel (quant_mlp_export.py:21-76).
+void linear_tc(sc_model *m, int layer, const int8_t *x, int64_t rows, int8_t *y, cudaStream_t s)
+{
+    if (rows <= 0) return;
+    const LayerDev &L = m->layers[layer];
+    const int kind = layer == 0 ? KK_LAYER0 : (layer == m->num_layers - 1 ? KK_LAST : KK_HIDDEN);
+    ProfScope ps(m->prof, kind, s, rows);
+    const int64_t row_tiles = (rows + TM - 1) / TM;
+    CUtensorMap xm = make_tmap(x, L.in_dim, rows, L.in_dim, TM);
+    const unsigned grid = (unsigned)std::min<int64_t>(row_tiles, m->num_sms);
+    L0Source src{};
+    k_layer<A_TMA><<<grid, 256, Cfg<A_TMA>::SMEM, s>>>(m->tc_wmaps[layer], xm, src, m->emb, L.bias, L.rq, y, rows,
+                                                      L.out_dim, L.in_dim, (int)row_tiles);
+    SC_LAUNCH_CHECK();
+    count_launch();
+}
+
 // Shared parameters of the fused kernels; activation buffers are sized for
 // grid * KT tiles of 128 rows.
 static void fused_common(sc_model *m, FusedParams &p, int grid, cudaStream_t s)

@@ -302,3 +302,23 @@ def test_decoder_runs_several_tiles_per_lane(lossless_model):
     # the persistent decoder is one launch (plus the start-of-sequence block and the
     # decoder-state set-up), whatever the number of chunks
     assert _lib.kernel_launches() - launches <= 4
+
+
+@pytest.mark.parametrize("layer", [0, 1, 8])
+@pytest.mark.parametrize("rows", [1, 127, 1000])
+def test_single_layer_matches_oracle(lossless_model, layer, rows):
+    """sc_linear_layer_device (one tcgen05 layer: the reference's bit_exact_linear_kernel,
+    quant_mlp_export.py:21-76) against the oracle's layer (cpu_int_inference.py:206-256)."""
+    import torch
+    from sigcomp_b200 import _lib
+    codec = _codec(lossless_model)
+    K = int(lossless_model.weights[layer].shape[1])
+    N = int(lossless_model.weights[layer].shape[0])
+    x = np.random.default_rng(rows + layer).integers(-128, 128, size=(rows, K)).astype(np.int8)
+    xd = torch.from_numpy(x).cuda()
+    y = torch.zeros((rows, N), dtype=torch.int8, device="cuda")
+    rc = codec._lib.sc_linear_layer_device(codec.handle, layer, ctypes.c_void_p(xd.data_ptr()), rows,
+                                           ctypes.c_void_p(y.data_ptr()),
+                                           ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    _lib.check(rc, "sc_linear_layer_device")
+    assert np.array_equal(y.cpu().numpy(), OracleModel(lossless_model).linear(x, layer))
