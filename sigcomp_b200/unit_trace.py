@@ -87,6 +87,7 @@ def main(argv=None):
     ap.add_argument("--chunk-len", type=int, default=2048)
     ap.add_argument("--records", type=int, default=400000, help="trace records kept per CTA")
     ap.add_argument("--gpu", type=int, default=0)
+    ap.add_argument("--dump", default=None, help="also save the raw records (npz: compress, decode)")
     args = ap.parse_args(argv)
 
     model = load_model(name="lossless")
@@ -115,6 +116,8 @@ def main(argv=None):
 
     (words, woff), rec_c = traced(lambda: codec.compress_flat(tokens, off))
     _, rec_d = traced(lambda: codec.decompress_flat(words, woff, np.diff(off)))
+    if args.dump:
+        np.savez_compressed(args.dump, compress=rec_c, decode=rec_d)
     print(f"configuration-2 generator, {args.reads} reads, {len(chunks)} chunks of <= {L} tokens, "
           f"{int(off[-1])} tokens; CTA 0 of the first SM pair")
     for name, rec in (("compress k_fused2<0>", rec_c), ("decode k_fused2<1>", rec_d)):
