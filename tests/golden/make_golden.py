@@ -24,6 +24,9 @@ Fixtures written:
   records.npz      - read records written by the reference's _write_read_payload and the SIDX
                      index entries (sigcomp/main.py:549-590, archive_shards.py:22);
                      `--only records` rewrites just this file
+  archive.npz      - int16 reads -> the reference's whole compress path to the record region, and
+                     that region back to signals (main.py:844-931, 1142-1165), lossless and lossy;
+                     `--only archive` rewrites just this file
 """
 
 import argparse
@@ -190,6 +193,70 @@ def _rna_streams(path):
     print("rna chunks", len(chunks), "tokens", len(tok), "words", sum(len(x) for x in streams) // 4)
 
 
+def _archive_cases(path):
+    """Whole read records of the archive's record region, both ways, from the reference's own code.
+
+    Compress (main.py:844-931): the lossy transform when lsb > 0, ``_split_signal``, the CPU codec's
+    ``batch_inference_reads``, ``_rice_compress`` of the large values and position deltas, and
+    ``_write_read_payload``.  Decompress (main.py:1142-1165): ``_parse_read_payload``,
+    ``batch_inference_reads`` on the framed streams, ``_reassemble_signal`` and the lossy decode.
+    Every delta of these reads fits a token (|delta| <= 127), so both rice blobs are the reference's
+    empty encoding (one zero byte, main.py:176-177) and fast_rice is never called.
+    """
+    import io
+    cc, ce, ci, sm = _import_reference(path)
+    model_dir = Path(path) / "sigcomp" / "pretrained_models"
+    rng = np.random.default_rng(44)
+    lengths = [9000, 4100, 2050, 2049, 2048, 700, 66, 65, 3, 2, 1]
+    out = {}
+    for name, lsb in (("lossless", 0), ("lossy", 3)):
+        codec = cc.CPUQuantMLPCompression(chunk_len=2048, model_path=str(model_dir / f"{name}.pth"),
+                                          inference_backend="int_mm", epilogue="numba", inference_batch_size=4096)
+        reads = []
+        for n in lengths:
+            d = np.clip(np.rint(rng.normal(0.0, 30.0, size=n - 1)), -127, 127).astype(np.int64)
+            reads.append((int(rng.integers(300, 700)) + np.concatenate([[0], np.cumsum(d)])).astype(np.int16))
+        recs = [sm.REC_FMT.pack(rng.bytes(16), float(rng.random()), float(rng.normal()), int(rng.integers(0, 256)),
+                                int(rng.integers(0, 256)), float(rng.random() * 5000), int(rng.integers(0, 2 ** 32)),
+                                int(rng.integers(0, 2 ** 32)), int(rng.integers(0, 2 ** 32)),
+                                int(rng.integers(0, 2 ** 62))) for _ in reads]
+        splits, small = [], []
+        for sig in reads:
+            if lsb > 0:
+                sig = sm._lossy_encode(sm._reduce_lsb(sig, lsb), lsb)
+            s = sm._split_signal(sig)
+            assert len(s[2]) == 0, "every delta fits a token"
+            splits.append(s)
+            small.append(s[1])
+        framed = codec.batch_inference_reads(list_of_reads=small, batch_size=1024, use_tqdm=False)
+        buf = io.BytesIO()
+        for rec, sig, (sig0, sv, l_adj, pos), s_bytes in zip(recs, reads, splits, framed):
+            sm._write_read_payload(buf, rec, sig0, len(sig), len(sv), s_bytes,
+                                   sm._rice_compress(l_adj, fallback_bits=16), sm._rice_compress(pos, fallback_bits=32))
+        region = buf.getvalue()
+        # back through the reference's reader and decoder
+        rd = io.BytesIO(region)
+        parsed = []
+        while (item := sm._parse_read_payload(rd)) is not None:
+            parsed.append(item)
+        decoded_small = codec.batch_inference_reads(list_of_compressed_reads=[p[1]["s_bytes"] for p in parsed],
+                                                    list_of_lengths=[p[1]["c_small"] for p in parsed],
+                                                    batch_size=4096, use_tqdm=False)
+        decoded = []
+        for (_, split), sv in zip(parsed, decoded_small):
+            sig = sm._reassemble_signal(split["sig0"], split["N"], sv, split["c_large"], split["l_bytes"],
+                                        split["p_bytes"])
+            decoded.append(sm._lossy_decode(sig, lsb) if lsb > 0 else sig)
+        out[f"{name}_lsb"] = np.asarray([lsb])
+        out[f"{name}_reads"] = np.concatenate(reads)
+        out[f"{name}_decoded"] = np.concatenate(decoded).astype(np.int16)
+        out[f"{name}_rec"] = np.frombuffer(b"".join(recs), dtype=np.uint8)
+        out[f"{name}_region"] = np.frombuffer(region, dtype=np.uint8)
+        print("archive", name, "reads", len(reads), "region bytes", len(region))
+    out["read_offsets"] = np.cumsum([0] + lengths).astype(np.int64)
+    np.savez_compressed(HERE / "archive.npz", **out)
+
+
 def _sharding_cases(path):
     """Read ranges of sample_balanced_ranges for edge cases and synthetic read sets."""
     sys.path.insert(0, str(path))
@@ -225,7 +292,7 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("SIGCOMP_REFERENCE", str(REPO / "baseline" / "_ref")),
                     help="root of the SigComp source tree (holding sigcomp/); default: $SIGCOMP_REFERENCE, "
                          "else the offline install under baseline/_ref")
-    ap.add_argument("--only", choices=["sharding", "records", "rna"], default=None)
+    ap.add_argument("--only", choices=["sharding", "records", "rna", "archive"], default=None)
     args = ap.parse_args()
     os.environ.setdefault("NUMBA_CACHE_DIR", "/tmp/nbcache")
     if args.only in (None, "sharding"):
@@ -234,6 +301,8 @@ def main():
         _record_cases(Path(args.reference))
     if args.only in (None, "rna"):
         _rna_streams(Path(args.reference))
+    if args.only in (None, "archive"):
+        _archive_cases(Path(args.reference))
     if args.only is not None:
         return
     cc, ce, ci, sm = _import_reference(Path(args.reference))

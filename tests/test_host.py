@@ -11,6 +11,7 @@ import pytest
 from oracle import signal
 from sigcomp_b200 import _lib, synthetic
 from conftest import REPO
+from oracle_backed import OracleBacked
 
 
 def _declared_symbols():
@@ -131,34 +132,6 @@ def test_framing_validation_errors():
         codec.compress_chunks([np.zeros(5, np.uint8)])
 
 
-class _OracleBacked:
-    """B200Compression's host framing with the CPU oracle in place of the two device calls
-    (compress_flat / decompress_flat), so that the framing alone is checked on the CPU."""
-
-    def __new__(cls, model, chunk_len=2048):
-        from sigcomp_b200.codec import B200Compression
-        from oracle.oracle import OracleModel
-        obj = object.__new__(B200Compression)
-        obj.chunk_len, obj.window_size, obj.SOS_token = chunk_len, 64, 256
-        om = OracleModel(model)
-
-        def compress_flat(tokens, offsets, stream=None):
-            chunks = [tokens[offsets[i]:offsets[i + 1]] for i in range(len(offsets) - 1)]
-            words = [np.frombuffer(s, "<u4") for s in om.compress_chunks(chunks, chunk_len, backend="int_mm")]
-            woff = np.zeros(len(words) + 1, np.int64)
-            np.cumsum([len(w) for w in words], out=woff[1:])
-            return np.concatenate(words + [np.zeros(0, "<u4")]).astype(np.uint32), woff
-
-        def decompress_flat(words, word_offsets, lengths, stream=None):
-            streams = [words[word_offsets[i]:word_offsets[i + 1]].astype("<u4").tobytes()
-                       for i in range(len(lengths))]
-            out = om.decompress_chunks(streams, [int(x) for x in lengths], chunk_len, backend="int_mm")
-            return np.concatenate(out + [np.zeros(0, np.uint8)])
-
-        obj.compress_flat, obj.decompress_flat = compress_flat, decompress_flat
-        return obj
-
-
 @pytest.mark.parametrize("name", ["lossless", "lossy", "rna"])
 def test_read_framing_matches_reference_golden_on_cpu(golden, name, request):
     """batch_inference_reads' chunking and '<H' framing reproduce the reference's framed reads
@@ -169,7 +142,7 @@ def test_read_framing_matches_reference_golden_on_cpu(golden, name, request):
     reads = [z["read_tokens"][o[i]:o[i + 1]] for i in range(len(o) - 1)]
     fo = z["framed_offsets"]
     framed_ref = [z["framed"][fo[i]:fo[i + 1]].tobytes() for i in range(len(reads))]
-    codec = _OracleBacked(model)
+    codec = OracleBacked(model)
     assert codec.batch_inference_reads(list_of_reads=reads) == framed_ref
     back = codec.batch_inference_reads(list_of_compressed_reads=framed_ref, list_of_lengths=[len(r) for r in reads])
     assert all(np.array_equal(a, b) for a, b in zip(back, reads))
