@@ -84,8 +84,11 @@ SC_API int sc_model_destroy(sc_model *model);
  * kernels on SM pairs for compress/decompress, the tcgen05 layer kernels for
  * sc_mlp_logits_device; a model they cannot run is refused with SC_ERR_UNSUPPORTED),
  * 1 = tcgen05 fused persistent kernels on SM pairs (cta_group::2), 2 = CUDA-core
- * kernels, 3 = tcgen05 one launch per layer, 4 = tcgen05 fused on single SMs.
- * Paths 2-4 are cross-checks of the same arithmetic, run only when selected here. */
+ * kernels, 3 = tcgen05 one launch per layer, 4 = tcgen05 fused on single SMs,
+ * 5 = as 1, with every decode on the small-batch decoder (a cluster of eight SMs per
+ * 128 chunks), which path 0 picks for batches of at most (SMs / 8) * 128 chunks and
+ * path 1 never.
+ * Paths 2-5 are cross-checks of the same arithmetic, run only when selected here. */
 SC_API int sc_model_set_mlp_path(sc_model *model, int32_t path);
 
 /*

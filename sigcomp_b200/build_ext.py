@@ -20,7 +20,7 @@ FLAGS = [
 # Kernels whose tcgen05.ld results land in registers asynchronously (until tcgen05.wait::ld):
 # a register spill placed between a load and its wait would store values not yet written, so the
 # build refuses any spill in them.  ptxas -v reports stack and spills per entry function.
-NO_SPILL_KERNELS = ("k_fused2",)
+NO_SPILL_KERNELS = ("k_fused2", "k_small_decode")
 NO_SPILL_SOURCE = "sc_mlp_tc.cu"
 
 

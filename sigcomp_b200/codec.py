@@ -87,7 +87,8 @@ class B200Compression:
         _lib.check(rc, "sc_model_create")
 
     def set_mlp_path(self, path):
-        code = {"auto": 0, "tcgen05": 1, "cuda_cores": 2, "tcgen05_layers": 3, "tcgen05_fused1": 4}[path]
+        code = {"auto": 0, "tcgen05": 1, "cuda_cores": 2, "tcgen05_layers": 3, "tcgen05_fused1": 4,
+                "tcgen05_small": 5}[path]
         _lib.check(self._lib.sc_model_set_mlp_path(self._handle, code), "sc_model_set_mlp_path")
         self.mlp_path = path
 

@@ -168,7 +168,9 @@ void fused_compress(sc_model *m, const int32_t *tile_chunk, const int32_t *tile_
                     cudaStream_t s);
 // Decode the chunks order[0 .. n_rows), sorted by length (descending, all nonzero; their
 // lengths on the host in sorted_len), with every layer and the decoder step in persistent
-// kernels: one launch on SM pairs, or launches of at most the single-SM kernels' capacity.
+// kernels: one launch on SM pairs, or, for a batch of at most num_sms / 8 tiles of 128 rows (or
+// with mlp_path 5), one launch with a cluster of eight CTAs per tile; or launches of at most the
+// single-SM kernels' capacity.
 void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int64_t *sorted_len,
                   const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
                   const int64_t *out_off, uint8_t *errors, cudaStream_t s);
@@ -182,7 +184,8 @@ struct sc_model {
     int device = 0;
     int32_t window = 64, emb_dim = 128, num_layers = 0, chunk_len = 2048;
     // 0 auto, 1 tcgen05 (fused, CTA pairs), 2 CUDA cores, 3 tcgen05 layer by layer,
-    // 4 tcgen05 fused on single CTAs
+    // 4 tcgen05 fused on single CTAs, 5 as 1 with every decode on the small-batch clusters
+    // (0 decodes batches of at most num_sms / 8 tiles there, 1 never)
     int32_t mlp_path = 0;
     int num_sms = 148;
     bool tc_ok = false;
@@ -191,6 +194,7 @@ struct sc_model {
     std::vector<sc::LayerDev> layers;
     std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path (box 256 rows)
     std::vector<CUtensorMap> tc_wmaps2;  // weight tensor maps for CTA pairs (box 128 rows)
+    std::vector<CUtensorMap> small_wmaps;  // small-batch decoder: box out_dim / 8 rows
     sc::Profiler prof;
     // unit trace of the first SM pair of the fused kernels (sc_trace_enable)
     unsigned long long *trace_buf = nullptr;
@@ -198,5 +202,5 @@ struct sc_model {
     int trace_cap = 0;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
-        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering, ws_sched;
+        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering, ws_sched, ws_small_logits;
 };

@@ -340,6 +340,7 @@ __global__ void __launch_bounds__(256, 1) k_layer(
 
 #include "sc_mlp_fused.cuh"
 #include "sc_mlp_fused2.cuh"
+#include "sc_mlp_small.cuh"
 
 namespace sc {
 namespace {
@@ -407,6 +408,12 @@ void mlp_tc_prepare(sc_model *m)
     maps2.clear();
     for (auto &L : m->layers) maps2.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, TN / 2));
     SC_CUDA(cudaFuncSetAttribute(k_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FCfg<false>::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_small_decode<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallCfg::SMEM));
+    SC_CUDA(cudaFuncSetAttribute(k_small_decode<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallCfg::SMEM));
+    auto &maps3 = m->small_wmaps;
+    maps3.clear();
+    for (auto &L : m->layers)
+        maps3.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, (uint32_t)(L.out_dim / SMALL_C)));
     SC_CUDA(cudaDeviceGetAttribute(&m->num_sms, cudaDevAttrMultiProcessorCount, m->device));
 }
 
@@ -649,12 +656,96 @@ static DecSchedule build_decode_schedule(const std::vector<int32_t> &pt_len, int
     return out;
 }
 
+// Small-batch decoding (sc_mlp_small.cuh): one cluster of SMALL_C CTAs per tile of 128 rows, as
+// many clusters as tiles up to one per SMALL_C SMs (further tiles run after those, in order).
+static void small_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int64_t *sorted_len,
+                         const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
+                         const int64_t *out_off, uint8_t *errors, cudaStream_t s)
+{
+    const int64_t n_tiles = (n_rows + TM - 1) / TM;
+    if (n_tiles > INT32_MAX / SMALL_C) throw CudaError{cudaErrorInvalidValue, "small_decode: too many rows"};
+    const int clusters = (int)std::min<int64_t>(n_tiles, std::max(1, m->num_sms / SMALL_C));
+    std::vector<int32_t> steps(n_tiles);
+    int64_t work = 0;
+    for (int64_t t = 0; t < n_tiles; ++t) steps[t] = (int32_t)sorted_len[t * TM];
+    for (int64_t j = 0; j < n_rows; ++j) work += sorted_len[j];
+    int32_t *d_steps = (int32_t *)m->ws_sched.get(sizeof(int32_t) * n_tiles, s);
+    SC_CUDA(cudaMemcpyAsync(d_steps, steps.data(), sizeof(int32_t) * n_tiles, cudaMemcpyHostToDevice, s));
+    ProfScope ps(m->prof, KK_FUSED_DECODE, s, work);
+    SmallParams p{};
+    const int64_t rows = (int64_t)clusters * TM;
+    int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
+    int8_t *a1 = (int8_t *)m->ws_act1.get((size_t)rows * MAX_N, s);
+    p.act_ptr[0] = a0;
+    p.act_ptr[1] = a1;
+    p.act[0] = make_tmap(a0, MAX_N, rows, MAX_N, TM);
+    p.act[1] = make_tmap(a1, MAX_N, rows, MAX_N, TM);
+    p.logits = (int8_t *)m->ws_small_logits.get((size_t)rows * SC_VOCAB, s);
+    // embedding ring: [clusters][WIN] blocks of 128 rows x 128 B, then the SOS block
+    const int64_t ring_rows = rows * WIN;
+    int8_t *ring = (int8_t *)m->ws_ering.get((size_t)(ring_rows + TM) * KB, s);
+    k_sos_block<<<1, TM * KB / 16, 0, s>>>(ring + ring_rows * KB, m->emb);
+    SC_LAUNCH_CHECK();
+    count_launch();
+    p.ering = make_tmap(ring, KB, ring_rows + TM, KB, TM);
+    p.ering_ptr = ring;
+    p.ering_sos_row = ring_rows;
+    p.num_layers = m->num_layers;
+    for (int l = 0; l < m->num_layers; ++l) {
+        p.w[l] = m->small_wmaps[l];
+        p.bias[l] = m->layers[l].bias;
+        p.rq[l] = m->layers[l].rq;
+        p.in_dim[l] = m->layers[l].in_dim;
+        p.out_dim[l] = m->layers[l].out_dim;
+    }
+    p.lut = m->lut;
+    p.emb = m->emb;
+    p.n_tiles = (int)n_tiles;
+    p.tile_steps = d_steps;
+    p.order = order;
+    p.n_rows = n_rows;
+    p.lengths = lengths;
+    p.state = state;
+    p.words = words;
+    p.tokens_out = tokens_out;
+    p.out_off = out_off;
+    p.errors = errors;
+    if (m->trace_cap > 0) {
+        SC_CUDA(cudaMemsetAsync(m->trace_count, 0, 8 * sizeof(unsigned int), s));
+        p.trace = m->trace_buf;
+        p.trace_count = m->trace_count;
+        p.trace_cap = m->trace_cap;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(clusters * SMALL_C));
+    cfg.blockDim = dim3(SMALL_THREADS);
+    cfg.dynamicSmemBytes = SmallCfg::SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = SMALL_C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (p.trace != nullptr) SC_CUDA(cudaLaunchKernelEx(&cfg, k_small_decode<true>, p));
+    else SC_CUDA(cudaLaunchKernelEx(&cfg, k_small_decode<false>, p));
+    SC_LAUNCH_CHECK();
+    count_launch();
+}
+
 void fused_decode(sc_model *m, const int64_t *order, int64_t n_rows, const int64_t *sorted_len,
                   const int64_t *lengths, DecState *state, const uint32_t *words, uint8_t *tokens_out,
                   const int64_t *out_off, uint8_t *errors, cudaStream_t s)
 {
     if (n_rows <= 0) return;
     const int64_t n_tiles = (n_rows + TM - 1) / TM;
+    if (use_pairs(m) && (m->mlp_path == 5 || (m->mlp_path == 0 && n_tiles * SMALL_C <= m->num_sms))) {
+        // too few tiles to fill the SM pairs' lanes: each tile on a cluster of eight SMs
+        // (path 1 keeps every batch on the pairs, path 5 puts every batch here: cross-checks)
+        small_decode(m, order, n_rows, sorted_len, lengths, state, words, tokens_out, out_off, errors, s);
+        return;
+    }
     if (use_pairs(m)) {
         // one launch for the whole batch: every pair-tile is queued on a lane of some SM pair
         const int64_t n_pt = (n_tiles + 1) / 2;

@@ -207,6 +207,16 @@ __device__ __forceinline__ void tma_load_2d_pair_hint(void *smem_dst, const void
         : "memory");
 }
 
+// Single-CTA load with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_hint(void *smem_dst, const void *tmap, uint64_t *bar, int32_t x, int32_t y,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint "
+        "[%0], [%1, {%3, %4}], [%2], %5;"
+        ::"r"(smem_u32(smem_dst)), "l"(tmap), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+        : "memory");
+}
+
 // L2 policy for data streamed once from DRAM: evict it first.
 __device__ __forceinline__ uint64_t l2_policy_evict_first() {
     uint64_t pol;

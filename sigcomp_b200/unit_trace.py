@@ -26,7 +26,8 @@ from .codec import B200Compression
 from .model import load_model
 from .synthetic import make_reads
 
-ROLES = {0: "producer", 1: "mma", 2: "epilogue", 3: "builder"}
+# role 3: the compress kernel's layer-0 builders, or the small-batch decoder's coder step (rank 0)
+ROLES = {0: "producer", 1: "mma", 2: "epilogue", 3: "build/coder"}
 
 
 def decode_records(rec):
@@ -84,6 +85,9 @@ def summarise(rec, num_layers):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--reads", type=int, default=6000, help="configuration-2 reads to code")
+    ap.add_argument("--config1", action="store_true",
+                    help="code configuration 1 instead (64 reads x 20,000 samples): its decode runs on the "
+                         "small-batch decoder, one cluster of eight SMs per 128 chunks")
     ap.add_argument("--chunk-len", type=int, default=2048)
     ap.add_argument("--records", type=int, default=400000, help="trace records kept per CTA")
     ap.add_argument("--gpu", type=int, default=0)
@@ -91,7 +95,8 @@ def main(argv=None):
     args = ap.parse_args(argv)
 
     model = load_model(name="lossless")
-    reads = make_reads("r10_lognormal", seed=5, count=args.reads)
+    reads = (make_reads("r10_config1", seed=5) if args.config1
+             else make_reads("r10_lognormal", seed=5, count=args.reads))
     L = args.chunk_len
     codec = B200Compression(chunk_len=L, gpu=args.gpu, model=model)
     chunks = []
@@ -118,11 +123,14 @@ def main(argv=None):
     _, rec_d = traced(lambda: codec.decompress_flat(words, woff, np.diff(off)))
     if args.dump:
         np.savez_compressed(args.dump, compress=rec_c, decode=rec_d)
-    print(f"configuration-2 generator, {args.reads} reads, {len(chunks)} chunks of <= {L} tokens, "
-          f"{int(off[-1])} tokens; CTA 0 of the first SM pair")
-    for name, rec in (("compress k_fused2<0>", rec_c), ("decode k_fused2<1>", rec_d)):
+    what = "configuration 1, 64 reads" if args.config1 else f"configuration-2 generator, {args.reads} reads"
+    print(f"{what}, {len(chunks)} chunks of <= {L} tokens, {int(off[-1])} tokens; CTA 0 of the first SM pair "
+          f"(of the first cluster for the small-batch decoder)")
+    dec = "decode k_small_decode" if args.config1 else "decode k_fused2<1>"
+    for name, rec in (("compress k_fused2<0>", rec_c), (dec, rec_d)):
         rows, frac, steps, span_us = summarise(rec, model.num_layers)
-        print(f"\n== {name}: {len(rec)} records over {span_us:.1f} us, steps seen {steps}")
+        print(f"\n== {name}: {len(rec)} records over {span_us:.1f} us, steps seen {steps} "
+              f"({span_us / max(steps, 1):.1f} us per step)")
         print(f"  {'role':9s} {'units':6s} {'n':>7s} {'wait us':>9s} {'work us':>9s} {'wait ms':>9s} {'work ms':>9s}")
         for r, c, n, w, k, tw, tk in rows:
             print(f"  {r:9s} {c:6s} {n:7d} {w:9.2f} {k:9.2f} {tw:9.2f} {tk:9.2f}")

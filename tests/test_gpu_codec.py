@@ -11,9 +11,9 @@ from oracle.oracle import OracleModel
 pytestmark = pytest.mark.gpu
 
 PATHS = ["tcgen05", "cuda_cores"]
-# every MLP implementation the library ships: fused on SM pairs, fused on single
-# SMs, one launch per layer, CUDA cores
-ALL_PATHS = ["tcgen05", "tcgen05_fused1", "tcgen05_layers", "cuda_cores"]
+# every MLP implementation the library ships: fused on SM pairs, the small-batch decoder
+# (clusters of eight SMs per tile), fused on single SMs, one launch per layer, CUDA cores
+ALL_PATHS = ["tcgen05", "tcgen05_small", "tcgen05_fused1", "tcgen05_layers", "cuda_cores"]
 
 
 def _chunks(z, tok="tokens", off="offsets"):
@@ -322,3 +322,74 @@ def test_single_layer_matches_oracle(lossless_model, layer, rows):
                                            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     _lib.check(rc, "sc_linear_layer_device")
     assert np.array_equal(y.cpu().numpy(), OracleModel(lossless_model).linear(x, layer))
+
+
+def _mixed_chunks(n, L, seed):
+    from oracle import signal
+    from sigcomp_b200 import synthetic
+    reads = synthetic.make_reads("r10_lognormal", seed=seed, count=max(4, n * L // 20000 + 2))
+    toks = np.concatenate([signal.split_signal(r)[1] for r in reads])
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(0, L + 1, size=n)
+    lens[rng.random(n) < 0.4] = L
+    off = np.zeros(n + 1, np.int64)
+    np.cumsum(lens, out=off[1:])
+    assert off[-1] <= len(toks)
+    return toks[:off[-1]], off, lens
+
+
+@pytest.mark.parametrize("n,L", [(700, 256), (5000, 64)])
+def test_small_batch_decoder_matches_pairs(lossless_model, n, L):
+    """Small batches decode on a cluster of eight SMs per 128-row tile: path 0 picks it for at
+    most SMs / 8 tiles, path 5 forces it (5,000 chunks: 40 tiles over the clusters, each cluster
+    taking several tiles in turn).  Against the pair kernel (path 1) and the input, with lengths
+    mixed inside and across tiles, empty chunks included; streams against the oracle on a sample."""
+    tokens, off, lens = _mixed_chunks(n, L, seed=n)
+    codec = _codec(lossless_model, chunk_len=L)
+    words, woff = codec.compress_flat(tokens, off)
+    sample = list(range(0, n, 97))
+    ref = OracleModel(lossless_model).compress_chunks([tokens[off[i]:off[i + 1]] for i in sample], chunk_len=L,
+                                                      backend="int_mm")
+    assert [words[woff[i]:woff[i + 1]].astype("<u4").tobytes() for i in sample] == ref
+    try:
+        for path in ("tcgen05_small", "tcgen05", "auto"):
+            codec.set_mlp_path(path)
+            assert np.array_equal(codec.decompress_flat(words, woff, lens), tokens), path
+    finally:
+        codec.set_mlp_path("auto")
+
+
+def test_small_batch_decoder_corrupt_streams(lossless_model):
+    """Damaged streams on the small-batch decoder end in the same per-chunk errors as on the pair
+    kernel: the reference's invalid-stream condition stops a chunk's decoding, the other chunks
+    of its tile decode on."""
+    from sigcomp_b200 import _lib
+    tokens, off, lens = _mixed_chunks(300, 256, seed=11)
+    codec = _codec(lossless_model, chunk_len=256)
+    words, woff = codec.compress_flat(tokens, off)
+    rng = np.random.default_rng(12)
+    bad = words.copy()
+    hit = rng.choice(len(bad), size=60, replace=False)
+    bad[hit] ^= rng.integers(1, 2 ** 32, size=60, dtype=np.uint64).astype(np.uint32)
+    got = {}
+    try:
+        for path in ("tcgen05_small", "tcgen05"):
+            codec.set_mlp_path(path)
+            out = np.zeros(max(int(lens.sum()), 1), np.uint8)
+            err = np.zeros(len(lens), np.uint8)
+            rc = codec._lib.sc_decompress_chunks(codec.handle, _lib_ptr(bad), _lib_ptr(woff), _lib_ptr(lens), len(lens),
+                                                 _lib_ptr(out), _lib_ptr(err), None)
+            got[path] = (rc, out.copy(), err.copy())
+    finally:
+        codec.set_mlp_path("auto")
+    rc_s, out_s, err_s = got["tcgen05_small"]
+    rc_p, out_p, err_p = got["tcgen05"]
+    assert rc_s == rc_p
+    assert np.array_equal(err_s, err_p) and err_s.any()
+    # chunks without an error decode identically
+    for i in np.flatnonzero(err_s == 0):
+        assert np.array_equal(out_s[off[i]:off[i + 1]], out_p[off[i]:off[i + 1]])
+
+
+def _lib_ptr(a):
+    return ctypes.c_void_p(a.ctypes.data)
