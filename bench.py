@@ -713,6 +713,11 @@ def main():
 
         roofline = fused_roofline("fused_decode", "k_fused2<1>: persistent autoregressive decoder on SM pairs "
                                                   "(9 tcgen05 int8 layers + frequency search + range decode)")
+        if roofline is None:
+            # a batch of at most SMs / 8 tiles of 128 chunks decodes on the small-batch clusters
+            roofline = fused_roofline("small_decode", "k_small_decode: small-batch autoregressive decoder, a "
+                                                      "cluster of 8 SMs per 128 chunks (9 tcgen05 int8 layers "
+                                                      "split 8 ways + frequency search + range decode)")
         roofline_c = fused_roofline("fused_compress", "k_fused2<0>: fused compress on SM pairs (9 tcgen05 int8 "
                                                       "layers + (cum, freq) selection)")
         if roofline is not None:

@@ -19,20 +19,28 @@
 //     epilogue runs the coder step of every row (the pair kernel's frequency pass, search and
 //     range-decoder update), appends the decoded tokens' embedding rows to the ring and releases
 //     the next step in every CTA (`rbar`).
-// Every buffer is reused only after a signal that proves its previous contents were consumed in
-// every CTA: a CTA reaches layer L of step s only after rank 0 released step s (rbar), which
-// rank 0 does only after every CTA sent its last-layer slice of step s-1, i.e. after all their
-// loads of step s-1 completed.  No TMA load uses cluster multicast; every wait is bounded.
+// Layer 0 of step s reads window positions 0..62 from ring slots written at earlier steps, so its
+// loads and MMAs start while rank 0 is still decoding step s-1 (its coder scratch and the
+// accumulator are separate TMEM columns); only position 63, the token being decoded, waits for
+// rank 0's release (rbar).  Every buffer is reused only after a signal that proves its previous
+// contents were consumed in every CTA: layer 0's MMAs of step s, hence its epilogue and all that
+// follows, come after rbar of step s-1, which rank 0 sends only after every CTA sent its
+// last-layer slice of step s-1, i.e. after all their loads of step s-1 completed; the ring slot
+// rank 0 writes at step s-1 held the token that layer 0 of step s-1 read first, in every CTA.
+// No TMA load uses cluster multicast; every wait is bounded.
 #pragma once
 
 namespace sc {
 
 constexpr int SMALL_C = 8;                           // CTAs per tile
-constexpr int SMALL_STAGES = 6;
+constexpr int SMALL_STAGES = 8;
 constexpr int SMALL_B_MAX = (MAX_N / SMALL_C) * KB;  // 8 KB: a 64-row weight slice of one K block
 constexpr int SMALL_STAGE = A_BYTES + SMALL_B_MAX;   // 24 KB
 constexpr int SMALL_THREADS = 32 * 6;                // producer, MMA, four epilogue warps
-constexpr int SMALL_TMEM_COLS = 256;                 // accumulator (64) and rank 0's coder scratch
+// TMEM: columns 0..255 are rank 0's coder scratch (packed logits, cached frequencies), the
+// accumulator (64 columns) lives after them, so a step's layer 0 can run during the coder step
+constexpr int SMALL_TMEM_COLS = 512;
+constexpr int SMALL_ACC_COL = 256;
 
 struct SmallParams {
     CUtensorMap w[FMAX_LAYERS];       // weights, box (out_dim / SMALL_C) rows x 128 B
@@ -82,7 +90,7 @@ __device__ __forceinline__ void small_trace(const SmallParams &p, unsigned int &
 }
 
 struct SmallCfg {
-    static constexpr int OFF_BIAS = SMALL_STAGES * SMALL_STAGE;          // 144 KB
+    static constexpr int OFF_BIAS = SMALL_STAGES * SMALL_STAGE;          // 192 KB
     static constexpr int OFF_LUT = OFF_BIAS + FMAX_LAYERS * MAX_N * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
     // full/empty per stage, acc_full, acc_empty, xbar[2], lbar, rbar, drain
@@ -176,50 +184,64 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
                         tma_load_2d_hint(st, &p.ering, bar, 0, row, ring_policy);
                     }
                 };
-                // the weights of the first stages go out before the operand is ready
-                for (int kb = 0; kb < pre; ++kb) {
+                auto acquire = [&](int kb) -> uint8_t * {       // stage of K block kb, with its weights
                     const uint32_t i = it + kb;
                     const int s = i % SMALL_STAGES;
-                    if (!mbar_wait_cluster(&empty[s], ((i / SMALL_STAGES) & 1) ^ 1)) {
-                        it += kb;
-                        return !(aborted = true);
-                    }
+                    if (!mbar_wait_cluster(&empty[s], ((i / SMALL_STAGES) & 1) ^ 1)) return nullptr;
                     uint8_t *st = smem + s * SMALL_STAGE;
                     mbar_arrive_expect_tx(&full[s], tx);
                     tma_load_2d(st + A_BYTES, &p.w[L], &full[s], kb * KB, (int)rank * ns);
-                }
-                if (L != 0) {
+                    return st;
+                };
+                auto bar_of = [&](int kb) { return &full[(it + kb) % SMALL_STAGES]; };
+                if (L == 0) {
+                    // window positions 0..62 hold tokens decoded at earlier steps, already in the
+                    // ring: only the last one (the token rank 0 is decoding now) waits for its
+                    // release, so this layer's loads and MMAs overlap the previous step's coder
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        uint8_t *st = acquire(kb);
+                        if (st == nullptr) {
+                            it += kb;
+                            return !(aborted = true);
+                        }
+                        if (kb == nkb - 1) {
+                            // rank 0 releases every step, a tile's last one too: every layer 0 but
+                            // the cluster's very first consumes one release
+                            if (!first && !mbar_wait_cluster(rbar, rw & 1)) {
+                                it += kb + 1;
+                                return !(aborted = true);
+                            }
+                            rw += first ? 0 : 1;
+                            first = false;
+                            small_trace<TRACE>(p, tn, 0, 1, L, step);
+                        }
+                        a_load(kb, st, bar_of(kb));
+                    }
+                } else {
+                    // the weights of the first stages go out before the operand is ready
+                    uint8_t *sts[SMALL_STAGES];
+                    for (int kb = 0; kb < pre; ++kb) {
+                        sts[kb] = acquire(kb);
+                        if (sts[kb] == nullptr) {
+                            it += kb;
+                            return !(aborted = true);
+                        }
+                    }
                     if (!mbar_wait_cluster(&xbar[xw & 1], (xw >> 1) & 1)) {
                         it += pre;
                         return !(aborted = true);
                     }
                     ++xw;
-                } else if (!first) {
-                    // rank 0 releases every step, the last one of a tile too: layer 0 of any step
-                    // but the cluster's very first waits for the previous step's release
-                    if (!mbar_wait_cluster(rbar, rw & 1)) {
-                        it += pre;
-                        return !(aborted = true);
+                    small_trace<TRACE>(p, tn, 0, 1, L, step);
+                    for (int kb = 0; kb < pre; ++kb) a_load(kb, sts[kb], bar_of(kb));
+                    for (int kb = pre; kb < nkb; ++kb) {
+                        uint8_t *st = acquire(kb);
+                        if (st == nullptr) {
+                            it += kb;
+                            return !(aborted = true);
+                        }
+                        a_load(kb, st, bar_of(kb));
                     }
-                    ++rw;
-                }
-                first = false;
-                small_trace<TRACE>(p, tn, 0, 1, L, step);
-                for (int kb = 0; kb < pre; ++kb) {
-                    const int s = (it + kb) % SMALL_STAGES;
-                    a_load(kb, smem + s * SMALL_STAGE, &full[s]);
-                }
-                for (int kb = pre; kb < nkb; ++kb) {
-                    const uint32_t i = it + kb;
-                    const int s = i % SMALL_STAGES;
-                    if (!mbar_wait_cluster(&empty[s], ((i / SMALL_STAGES) & 1) ^ 1)) {
-                        it += kb;
-                        return !(aborted = true);
-                    }
-                    uint8_t *st = smem + s * SMALL_STAGE;
-                    mbar_arrive_expect_tx(&full[s], tx);
-                    tma_load_2d(st + A_BYTES, &p.w[L], &full[s], kb * KB, (int)rank * ns);
-                    a_load(kb, st, &full[s]);
                 }
                 it += nkb;
                 small_trace<TRACE>(p, tn, 0, 2, L, step);
@@ -254,7 +276,8 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
                     const uint32_t st = smem_u32(smem + s * SMALL_STAGE);
 #pragma unroll
                     for (int k = 0; k < KB / 32; ++k)
-                        mma_i8(tmem_base, smem_desc_sw128(st + 32 * k), smem_desc_sw128(st + A_BYTES + 32 * k), idesc,
+                        mma_i8(tmem_base + SMALL_ACC_COL, smem_desc_sw128(st + 32 * k),
+                               smem_desc_sw128(st + A_BYTES + 32 * k), idesc,
                                (kb || k) ? 1u : 0u);
                     mma_commit(&empty[s]);
                 }
@@ -271,7 +294,8 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
         // ---- epilogue warps: TMEM lane quarter q holds rows q*32 .. q*32+31 of the tile
         const int q = warp & 3;
         const int r = q * 32 + lane;
-        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16);   // coder scratch (rank 0)
+        const uint32_t tacc = taddr + SMALL_ACC_COL;                       // accumulator
         uint32_t ue = 0, lw = 0, xe = 0;
         unsigned int tn2 = 0, tn3 = 0;
         const bool tr = warp == 2 && lane == 0;
@@ -310,7 +334,7 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             // requantise this CTA's ns columns of the row: 32 (the last layer) or 64, in two halves
             auto requant32 = [&](int h, uint32_t (&out)[8]) {
                 uint32_t va[32];
-                tmem_ld32(taddr + h * 32, va);
+                tmem_ld32(tacc + h * 32, va);
                 tmem_ld_wait();
                 const int4 *bv = reinterpret_cast<const int4 *>(bias + h * 32);
 #pragma unroll
@@ -321,12 +345,10 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             uint32_t lo[8], hi[8];
             requant32(0, lo);
             if (ns > 32) requant32(1, hi);
-            if (!last || rank != 0) {
-                // the accumulator is read: the next layer's MMA may overwrite it
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(acc_empty);
-            }
+            // the accumulator is read: the next layer's MMA may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
             if (!last) {
                 int8_t *dst = p.act_ptr[L & 1] + (size_t)(row0 + r) * MAX_N + (int)rank * ns;
                 st_global_v8(dst, lo);
@@ -351,11 +373,15 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             if (tr) small_trace<TRACE>(p, tn3, 3, 1, L, step);
             int mlogit = -128;
             {
+                // all sixteen loads in flight at once (L2: the slices come from eight SMs)
                 const uint4 *src = reinterpret_cast<const uint4 *>(p.logits + (size_t)(row0 + r) * SC_VOCAB);
-#pragma unroll 1
+                uint4 v[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) v[i] = __ldcg(src + i);
+#pragma unroll
                 for (int c = 0; c < 8; ++c) {
-                    const uint4 a = __ldcg(src + 2 * c), b = __ldcg(src + 2 * c + 1);
-                    const uint32_t w8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+                    const uint32_t w8[8] = {v[2 * c].x, v[2 * c].y, v[2 * c].z, v[2 * c].w,
+                                            v[2 * c + 1].x, v[2 * c + 1].y, v[2 * c + 1].z, v[2 * c + 1].w};
 #pragma unroll
                     for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -397,10 +423,8 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             fence_proxy_async_global();              // the ring block is read by TMA next step
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(acc_empty);
+            if (lane == 0)
                 for (int c = 0; c < SMALL_C; ++c) mbar_arrive_cluster(map_to_rank(rbar, (uint32_t)c));
-            }
             if (tr) small_trace<TRACE>(p, tn3, 3, 2, L, step);
             return true;
         });

@@ -671,7 +671,7 @@ static void small_decode(sc_model *m, const int64_t *order, int64_t n_rows, cons
     for (int64_t j = 0; j < n_rows; ++j) work += sorted_len[j];
     int32_t *d_steps = (int32_t *)m->ws_sched.get(sizeof(int32_t) * n_tiles, s);
     SC_CUDA(cudaMemcpyAsync(d_steps, steps.data(), sizeof(int32_t) * n_tiles, cudaMemcpyHostToDevice, s));
-    ProfScope ps(m->prof, KK_FUSED_DECODE, s, work);
+    ProfScope ps(m->prof, KK_SMALL_DECODE, s, work);
     SmallParams p{};
     const int64_t rows = (int64_t)clusters * TM;
     int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
