@@ -262,7 +262,7 @@ int sc_model_destroy(sc_model *m)
         }
         for (DevBuf *b : {&m->ws_windows, &m->ws_act0, &m->ws_act1, &m->ws_logits, &m->ws_pairs, &m->ws_stage,
                           &m->ws_nwords, &m->ws_err, &m->ws_scan, &m->ws_tmp, &m->ws_order, &m->ws_state,
-                          &m->ws_tok_off, &m->ws_misc, &m->ws_ering, &m->ws_sched, &m->ws_small_logits})
+                          &m->ws_tok_off, &m->ws_misc, &m->ws_ering, &m->ws_sched})
             b->release();
     }
     delete m;

@@ -203,5 +203,5 @@ struct sc_model {
     int trace_cap = 0;
     // workspaces
     sc::DevBuf ws_windows, ws_act0, ws_act1, ws_logits, ws_pairs, ws_stage, ws_nwords,
-        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering, ws_sched, ws_small_logits;
+        ws_err, ws_scan, ws_tmp, ws_order, ws_state, ws_tok_off, ws_misc, ws_ering, ws_sched;
 };

@@ -4,38 +4,46 @@
 // a step's nine dependent layers behind the other tiles of its SM.  A batch of a few hundred
 // chunks has too few tiles for that: three SM pairs would run one tile each, one step every
 // ~110 us.  Here every tile runs on a cluster of eight CTAs instead, each computing 1/8 of every
-// layer's outputs (N = 64 of 512, 32 of the last layer's 256), so a step's MMA work is spread over
-// eight SMs:
-//   - every CTA loads the full A operand of a layer (the embedding ring for layer 0, the previous
-//     layer's activations otherwise) and its own N-slice of the weights, by TMA;
-//   - its epilogue writes its slice of the layer's output to the cluster's activation rows in
-//     global memory (L2) and arrives on an `xbar` mbarrier of every CTA of the cluster, whose
-//     producers wait for all eight slices before loading the next layer.  Consecutive exchanges
-//     alternate between two barriers: a warp makes its eight arrivals for exchange k before its
-//     CTA can start on exchange k+1, but another CTA's barrier may not have seen them all yet,
-//     and an arrival for k+1 must never count toward k there; one for k+2 cannot come before
-//     every CTA has seen all of k+1, hence all of k;
-//   - the last layer's logit slices are gathered the same way in rank 0 (`lbar`), whose
+// layer's outputs (N = 64 of 512, 32 of the last layer's 256), so a step's work is spread over
+// eight SMs, and a layer's output slices are exchanged in distributed shared memory:
+//   - every CTA holds the tile's activations in two resident buffers (B0, B1: 128 rows x 512 B,
+//     four 128-byte-swizzled K blocks, the MMA's A operand layout); layer L >= 1 reads
+//     B[(L-1) & 1], and the epilogue of layer L < 8 writes its 64-column slice into B[L & 1] of
+//     every CTA of the cluster (st.shared::cluster), then arrives on an `xbar` mbarrier of every
+//     CTA, on which that CTA's MMA issuer waits before the next layer;
+//   - consecutive exchanges alternate between two barriers: a warp makes its eight arrivals for
+//     exchange k before its CTA can start on exchange k+1, but another CTA's barrier may not have
+//     seen them all yet, and an arrival for k+1 must never count toward k there; one for k+2
+//     cannot come before every CTA has seen all of k+1, hence all of k;
+//   - the producer streams only weights for layers >= 1 (8 KB per K block, a ring that runs up
+//     to 2.5 layers ahead); layer 0's A operand, the 64-token window, comes by TMA from the
+//     cluster's embedding ring in global memory through 24 KB stages that overlay B1, which is
+//     free during layer 0 (the producer switches between the two stage rings only after the one
+//     it leaves is consumed: every MMA that read it, and hence layer 8's reads of B1, completed);
+//   - the last layer's logit slices are gathered in rank 0's B0, free by then (`lbar`); rank 0's
 //     epilogue runs the coder step of every row (the pair kernel's frequency pass, search and
 //     range-decoder update), appends the decoded tokens' embedding rows to the ring and releases
 //     the next step in every CTA (`rbar`).
 // Layer 0 of step s reads window positions 0..62 from ring slots written at earlier steps, so its
 // loads and MMAs start while rank 0 is still decoding step s-1 (its coder scratch and the
 // accumulator are separate TMEM columns); only position 63, the token being decoded, waits for
-// rank 0's release (rbar).  Every buffer is reused only after a signal that proves its previous
-// contents were consumed in every CTA: layer 0's MMAs of step s, hence its epilogue and all that
-// follows, come after rbar of step s-1, which rank 0 sends only after every CTA sent its
-// last-layer slice of step s-1, i.e. after all their loads of step s-1 completed; the ring slot
-// rank 0 writes at step s-1 held the token that layer 0 of step s-1 read first, in every CTA.
-// No TMA load uses cluster multicast; every wait is bounded.
+// rbar.  Every buffer is written only after a signal that proves its previous contents consumed
+// in every CTA: a CTA writes B[L & 1] at layer L after its own layer-L MMAs, which waited for
+// every CTA's layer L-1 slices, each sent after that CTA's layer L-1 MMAs (the last readers of
+// B[L & 1]) completed; layer 0's writes to B0 come after rbar of the previous step, which rank 0
+// sends after the coder has read the logits out of its B0.  No TMA load uses cluster multicast;
+// every wait is bounded.
 #pragma once
 
 namespace sc {
 
 constexpr int SMALL_C = 8;                           // CTAs per tile
-constexpr int SMALL_STAGES = 8;
-constexpr int SMALL_B_MAX = (MAX_N / SMALL_C) * KB;  // 8 KB: a 64-row weight slice of one K block
-constexpr int SMALL_STAGE = A_BYTES + SMALL_B_MAX;   // 24 KB
+constexpr int SMALL_NS = MAX_N / SMALL_C;            // 64 output columns per CTA (hidden layers)
+constexpr int SMALL_B = TM * MAX_N;                  // 64 KB: one resident activation buffer
+constexpr int SMALL_ST0 = A_BYTES + SMALL_NS * KB;   // 24 KB: a layer-0 stage (ring block + weights)
+constexpr int SMALL_STAGES0 = 6;                     // layer-0 stages, over B1 and beyond
+constexpr int SMALL_ST1 = SMALL_NS * KB;             // 8 KB: a weight slice of one K block
+constexpr int SMALL_STAGES1 = 10;                    // weight stages of layers >= 1
 constexpr int SMALL_THREADS = 32 * 6;                // producer, MMA, four epilogue warps
 // TMEM: columns 0..255 are rank 0's coder scratch (packed logits, cached frequencies), the
 // accumulator (64 columns) lives after them, so a step's layer 0 can run during the coder step
@@ -44,10 +52,7 @@ constexpr int SMALL_ACC_COL = 256;
 
 struct SmallParams {
     CUtensorMap w[FMAX_LAYERS];       // weights, box (out_dim / SMALL_C) rows x 128 B
-    CUtensorMap act[2];               // activation ping-pong [clusters * 128][512], box 128 x 128 B
     CUtensorMap ering;                // embedding ring, box 128 rows x 128 B
-    int8_t *act_ptr[2];
-    int8_t *logits;                   // [clusters * 128][256]: the last layer's requantised logits
     int8_t *ering_ptr;                // [clusters][WIN][128][128], then the start-of-sequence block
     int64_t ering_sos_row;
     const int32_t *bias[FMAX_LAYERS];
@@ -90,12 +95,19 @@ __device__ __forceinline__ void small_trace(const SmallParams &p, unsigned int &
 }
 
 struct SmallCfg {
-    static constexpr int OFF_BIAS = SMALL_STAGES * SMALL_STAGE;          // 192 KB
-    static constexpr int OFF_LUT = OFF_BIAS + FMAX_LAYERS * MAX_N * 4;
+    static constexpr int OFF_B0 = 0;
+    static constexpr int OFF_B1 = SMALL_B;                               // 64 KB
+    static constexpr int OFF_RING0 = OFF_B1;                             // layer-0 stages over B1...
+    static constexpr int OFF_RING1 = OFF_B1 + SMALL_B;                   // ...weight stages after it
+    static constexpr int END_RINGS = OFF_RING0 + SMALL_STAGES0 * SMALL_ST0;   // 208 KB
+    static_assert(OFF_RING1 + SMALL_STAGES1 * SMALL_ST1 <= END_RINGS, "weight stages inside the ring area");
+    static constexpr int OFF_BIAS = END_RINGS;                           // this CTA's bias slices
+    static constexpr int OFF_LUT = OFF_BIAS + FMAX_LAYERS * SMALL_NS * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
-    // full/empty per stage, acc_full, acc_empty, xbar[2], lbar, rbar, drain
-    static constexpr int NBAR = 2 * SMALL_STAGES + 7;
-    static constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+    // full/empty of both rings, acc_full, acc_empty, xbar[2], lbar, rbar, drain
+    static constexpr int NBAR = 2 * SMALL_STAGES0 + 2 * SMALL_STAGES1 + 7;
+    static constexpr int OFF_CNT = OFF_BAR + NBAR * 8;                   // epilogue warps' slice counter
+    static constexpr int OFF_TMEM = OFF_CNT + 16;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;
     static_assert(SMEM <= 232448, "shared memory per CTA");
 };
@@ -113,6 +125,35 @@ __device__ __forceinline__ void for_each_small_unit(const SmallParams &p, F &&f)
     }
 }
 
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory to the shared memory of a
+// CTA of the cluster, completing on an mbarrier of that CTA (both shared::cluster addresses): the
+// copy engine moves a whole slice with one instruction, where per-thread remote stores would each
+// pay the cluster network's round trip.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst_cluster, const void *src, uint32_t bytes,
+                                                     uint32_t bar_cluster)
+{
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(dst_cluster), "r"(smem_u32(src)), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+
+// K-major operand without swizzle: 8-row x 16-byte core matrices of 128 contiguous bytes, the
+// core matrices of one 16-byte K chunk stacked over the rows at `sbo` bytes, consecutive K chunks
+// `lbo` bytes apart.  The resident activation buffers use lbo = 2048 (a K chunk of all 128 rows)
+// and sbo = 128, so byte k of row r sits at (k / 16) * 2048 + r * 16 + k % 16 and a CTA's 64
+// columns are one contiguous 8 KB block.
+__device__ __forceinline__ uint64_t smem_desc_noswz(uint32_t smem_addr, uint32_t lbo, uint32_t sbo)
+{
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr & 0x3FFFF) >> 4);       // start address  [0,14)
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;         // leading byte offset: next K core matrix
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;         // stride byte offset: next 8 rows
+    d |= (uint64_t)1 << 46;                             // descriptor version (sm_100)
+    return d;                                           // swizzle mode 0: none
+}
+
+constexpr int SMALL_KCHUNK = TM * 16;                // 2 KB: one 16-byte K chunk of all 128 rows
+
 template <bool TRACE>
 __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_constant__ SmallParams p)
 {
@@ -120,32 +161,41 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t *bars = (uint64_t *)(smem + C::OFF_BAR);
-    uint64_t *full = bars, *empty = bars + SMALL_STAGES;
-    uint64_t *acc_full = bars + 2 * SMALL_STAGES, *acc_empty = acc_full + 1;
-    uint64_t *xbar = acc_empty + 1;   // [2]: all CTAs' slices of a layer's output are in L2
-    uint64_t *lbar = xbar + 2;        // rank 0: all CTAs' last-layer logit slices are in L2
+    uint64_t *full0 = bars, *empty0 = full0 + SMALL_STAGES0;       // layer-0 stages
+    uint64_t *full1 = empty0 + SMALL_STAGES0, *empty1 = full1 + SMALL_STAGES1;   // weight stages
+    uint64_t *acc_full = empty1 + SMALL_STAGES1, *acc_empty = acc_full + 1;
+    uint64_t *xbar = acc_empty + 1;   // [2]: every CTA's slice of a layer's output is in this CTA's buffer
+    uint64_t *lbar = xbar + 2;        // rank 0: every CTA's last-layer logit slice is in its B0
     uint64_t *rbar = lbar + 1;        // rank 0 appended the step's tokens to the ring
     uint64_t *drain = rbar + 1;       // the MMA issuer's last commit: TMEM is freed after it
     uint32_t *tmem_slot = (uint32_t *)(smem + C::OFF_TMEM);
+    // +1 per epilogue warp once its rows of a unit's output slice are in this CTA's shared memory
+    uint32_t *slice_cnt = (uint32_t *)(smem + C::OFF_CNT);
     int32_t *bias_s = (int32_t *)(smem + C::OFF_BIAS);
     uint64_t *lut_s = (uint64_t *)(smem + C::OFF_LUT);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NL = p.num_layers;
     const uint32_t rank = cluster_ctarank();
-    const int row0 = (blockIdx.x / SMALL_C) * TM;     // this cluster's activation / logit / ring rows
+    const int ring_block0 = (blockIdx.x / SMALL_C) * WIN;   // this cluster's first embedding-ring block
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SMALL_STAGES; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < SMALL_STAGES0; ++s) {
+            mbar_init(&full0[s], 1);
+            mbar_init(&empty0[s], 1);
+        }
+        for (int s = 0; s < SMALL_STAGES1; ++s) {
+            mbar_init(&full1[s], 1);
+            mbar_init(&empty1[s], 1);
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 4);
-        mbar_init(&xbar[0], 4 * SMALL_C);              // four epilogue warps of every CTA
-        mbar_init(&xbar[1], 4 * SMALL_C);
-        mbar_init(lbar, 4 * SMALL_C);
+        // the exchanges: one local arrival (with the bytes the seven peers' copies bring)
+        mbar_init(&xbar[0], 1);
+        mbar_init(&xbar[1], 1);
+        mbar_init(lbar, 1);
         mbar_init(rbar, 4);                            // rank 0's epilogue warps
         mbar_init(drain, 1);
+        *slice_cnt = 0;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -153,133 +203,140 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
         tmem_relinquish();
     }
     for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = p.lut[i];
-    for (int l = 0; l < NL; ++l)
-        for (int i = threadIdx.x; i < p.out_dim[l]; i += blockDim.x) bias_s[l * MAX_N + i] = p.bias[l][i];
+    for (int l = 0; l < NL; ++l) {
+        const int ns = p.out_dim[l] / SMALL_C;
+        for (int i = threadIdx.x; i < ns; i += blockDim.x) bias_s[l * SMALL_NS + i] = p.bias[l][(int)rank * ns + i];
+    }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();                   // every CTA's barriers exist before any remote arrival
+    cluster_sync();                   // every CTA's barriers exist before any remote arrival or store
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---- TMA producer: the full A operand and this CTA's N-slice of the weights
-            uint32_t it = 0, xw = 0, rw = 0;
+            // ---- TMA producer: layer 0's window blocks and weights, the other layers' weights
+            uint32_t it0 = 0, it1 = 0, rw = 0;           // blocks issued per stage ring, rbar waits
+            int last_ring = -1;
             unsigned int tn = 0;
             bool aborted = false, first = true;
             const uint64_t ring_policy = l2_policy_evict_first();
             for_each_small_unit(p, [&](int tile, int step, int L) -> bool {
                 const int nkb = p.in_dim[L] / KB;
                 const int ns = p.out_dim[L] / SMALL_C;
-                const uint32_t tx = A_BYTES + ns * KB;
-                const int pre = nkb < SMALL_STAGES ? nkb : SMALL_STAGES;
+                const int rg = L == 0 ? 0 : 1;
                 small_trace<TRACE>(p, tn, 0, 0, L, step);
-                auto a_load = [&](int kb, uint8_t *st, uint64_t *bar) {
-                    if (L != 0) {
-                        tma_load_2d(st, &p.act[(L - 1) & 1], bar, kb * KB, row0);
-                    } else {
-                        // window position kb holds token step - 64 + kb (start-of-sequence before 0)
-                        const int tau = step - WIN + kb;
-                        const int row = tau < 0 ? (int)p.ering_sos_row : (row0 / TM * WIN + (tau & (WIN - 1))) * TM;
-                        tma_load_2d_hint(st, &p.ering, bar, 0, row, ring_policy);
-                    }
-                };
-                auto acquire = [&](int kb) -> uint8_t * {       // stage of K block kb, with its weights
-                    const uint32_t i = it + kb;
-                    const int s = i % SMALL_STAGES;
-                    if (!mbar_wait_cluster(&empty[s], ((i / SMALL_STAGES) & 1) ^ 1)) return nullptr;
-                    uint8_t *st = smem + s * SMALL_STAGE;
-                    mbar_arrive_expect_tx(&full[s], tx);
-                    tma_load_2d(st + A_BYTES, &p.w[L], &full[s], kb * KB, (int)rank * ns);
-                    return st;
-                };
-                auto bar_of = [&](int kb) { return &full[(it + kb) % SMALL_STAGES]; };
+                if (rg != last_ring && last_ring >= 0) {
+                    // the two rings share memory: the one left behind is consumed (its last
+                    // block's MMAs completed, and MMAs complete in order) before the other refills it
+                    const uint32_t i = (last_ring ? it1 : it0) - 1;
+                    const bool ok = last_ring ? mbar_wait_cluster(&empty1[i % SMALL_STAGES1], (i / SMALL_STAGES1) & 1)
+                                              : mbar_wait_cluster(&empty0[i % SMALL_STAGES0], (i / SMALL_STAGES0) & 1);
+                    if (!ok) return !(aborted = true);
+                }
+                last_ring = rg;
                 if (L == 0) {
-                    // window positions 0..62 hold tokens decoded at earlier steps, already in the
-                    // ring: only the last one (the token rank 0 is decoding now) waits for its
-                    // release, so this layer's loads and MMAs overlap the previous step's coder
                     for (int kb = 0; kb < nkb; ++kb) {
-                        uint8_t *st = acquire(kb);
-                        if (st == nullptr) {
-                            it += kb;
-                            return !(aborted = true);
-                        }
+                        const int s = it0 % SMALL_STAGES0;
+                        if (!mbar_wait_cluster(&empty0[s], ((it0 / SMALL_STAGES0) & 1) ^ 1)) return !(aborted = true);
+                        uint8_t *st = smem + C::OFF_RING0 + s * SMALL_ST0;
+                        mbar_arrive_expect_tx(&full0[s], A_BYTES + ns * KB);
+                        tma_load_2d(st + A_BYTES, &p.w[0], &full0[s], kb * KB, (int)rank * ns);
+                        ++it0;
                         if (kb == nkb - 1) {
-                            // rank 0 releases every step, a tile's last one too: every layer 0 but
-                            // the cluster's very first consumes one release
-                            if (!first && !mbar_wait_cluster(rbar, rw & 1)) {
-                                it += kb + 1;
-                                return !(aborted = true);
-                            }
+                            // window positions 0..62 hold tokens of earlier steps, already in the
+                            // ring; the last one is the token rank 0 is decoding now.  Rank 0
+                            // releases every step, a tile's last one too: every layer 0 but the
+                            // cluster's very first consumes one release.
+                            if (!first && !mbar_wait_cluster(rbar, rw & 1)) return !(aborted = true);
                             rw += first ? 0 : 1;
                             first = false;
                             small_trace<TRACE>(p, tn, 0, 1, L, step);
                         }
-                        a_load(kb, st, bar_of(kb));
+                        // window position kb holds token step - 64 + kb (start-of-sequence before 0)
+                        const int tau = step - WIN + kb;
+                        const int row = tau < 0 ? (int)p.ering_sos_row : (ring_block0 + (tau & (WIN - 1))) * TM;
+                        tma_load_2d_hint(st, &p.ering, &full0[s], 0, row, ring_policy);
                     }
                 } else {
-                    // the weights of the first stages go out before the operand is ready
-                    uint8_t *sts[SMALL_STAGES];
-                    for (int kb = 0; kb < pre; ++kb) {
-                        sts[kb] = acquire(kb);
-                        if (sts[kb] == nullptr) {
-                            it += kb;
-                            return !(aborted = true);
-                        }
-                    }
-                    if (!mbar_wait_cluster(&xbar[xw & 1], (xw >> 1) & 1)) {
-                        it += pre;
-                        return !(aborted = true);
-                    }
-                    ++xw;
                     small_trace<TRACE>(p, tn, 0, 1, L, step);
-                    for (int kb = 0; kb < pre; ++kb) a_load(kb, sts[kb], bar_of(kb));
-                    for (int kb = pre; kb < nkb; ++kb) {
-                        uint8_t *st = acquire(kb);
-                        if (st == nullptr) {
-                            it += kb;
-                            return !(aborted = true);
-                        }
-                        a_load(kb, st, bar_of(kb));
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const int s = it1 % SMALL_STAGES1;
+                        if (!mbar_wait_cluster(&empty1[s], ((it1 / SMALL_STAGES1) & 1) ^ 1)) return !(aborted = true);
+                        uint8_t *st = smem + C::OFF_RING1 + s * SMALL_ST1;
+                        mbar_arrive_expect_tx(&full1[s], ns * KB);
+                        tma_load_2d(st, &p.w[L], &full1[s], kb * KB, (int)rank * ns);
+                        ++it1;
                     }
                 }
-                it += nkb;
                 small_trace<TRACE>(p, tn, 0, 2, L, step);
                 return true;
             });
             if (TRACE && blockIdx.x < 2) p.trace_count[blockIdx.x * 4 + 0] = tn;
             if (aborted) {
                 // loads already issued may still be landing in shared memory: wait (bounded) for the
-                // full phases of the last stages, then give stragglers time before the CTA ends
-                for (uint32_t i = it > (uint32_t)SMALL_STAGES ? it - SMALL_STAGES : 0; i < it; ++i)
-                    mbar_wait_cluster_drain(&full[i % SMALL_STAGES], (i / SMALL_STAGES) & 1);
+                // full phases of each ring's last stages, then give stragglers time before the CTA ends
+                for (uint32_t i = it0 > (uint32_t)SMALL_STAGES0 ? it0 - SMALL_STAGES0 : 0; i < it0; ++i)
+                    mbar_wait_cluster_drain(&full0[i % SMALL_STAGES0], (i / SMALL_STAGES0) & 1);
+                for (uint32_t i = it1 > (uint32_t)SMALL_STAGES1 ? it1 - SMALL_STAGES1 : 0; i < it1; ++i)
+                    mbar_wait_cluster_drain(&full1[i % SMALL_STAGES1], (i / SMALL_STAGES1) & 1);
                 spin_ns(100000);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---- MMA issuer: D[128 x ns] = A[128 x K] * W_slice[ns x K]^T, one accumulator
-            uint32_t it = 0, uu = 0;
+            uint32_t it0 = 0, it1 = 0, uu = 0, xm = 0;
             unsigned int tn = 0;
+            const uint32_t d = tmem_base + SMALL_ACC_COL;
             for_each_small_unit(p, [&](int tile, int step, int L) -> bool {
                 const int nkb = p.in_dim[L] / KB;
-                const int ns = p.out_dim[L] / SMALL_C;
-                const uint32_t idesc = idesc_i8(TM, ns);
+                const uint32_t idesc = idesc_i8(TM, p.out_dim[L] / SMALL_C);
                 small_trace<TRACE>(p, tn, 1, 0, L, step);
                 if (!mbar_wait_cluster(acc_empty, (uu & 1) ^ 1)) return false;
+                if (L != 0) {
+                    // every CTA's slice of layer L-1's output is in this CTA's buffer
+                    if (!mbar_wait_cluster(&xbar[xm & 1], (xm >> 1) & 1)) return false;
+                    ++xm;
+                }
                 small_trace<TRACE>(p, tn, 1, 1, L, step);
                 tc_fence_after();
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % SMALL_STAGES;
-                    if (!mbar_wait_cluster(&full[s], (it / SMALL_STAGES) & 1)) return false;
-                    tc_fence_after();
-                    const uint32_t st = smem_u32(smem + s * SMALL_STAGE);
+                if (L == 0) {
+                    for (int kb = 0; kb < nkb; ++kb, ++it0) {
+                        const int s = it0 % SMALL_STAGES0;
+                        if (!mbar_wait_cluster(&full0[s], (it0 / SMALL_STAGES0) & 1)) return false;
+                        tc_fence_after();
+                        const uint32_t st = smem_u32(smem + C::OFF_RING0 + s * SMALL_ST0);
 #pragma unroll
-                    for (int k = 0; k < KB / 32; ++k)
-                        mma_i8(tmem_base + SMALL_ACC_COL, smem_desc_sw128(st + 32 * k),
-                               smem_desc_sw128(st + A_BYTES + 32 * k), idesc,
-                               (kb || k) ? 1u : 0u);
-                    mma_commit(&empty[s]);
+                        for (int k = 0; k < KB / 32; ++k)
+                            mma_i8(d, smem_desc_sw128(st + 32 * k), smem_desc_sw128(st + A_BYTES + 32 * k), idesc,
+                                   (kb || k) ? 1u : 0u);
+                        mma_commit(&empty0[s]);
+                    }
+                } else {
+                    // K block kb of the resident buffer: K chunks 8 kb .. 8 kb + 7, two per MMA.
+                    // The weights are streamed well ahead: wait for all of the layer's blocks, then
+                    // issue its MMAs back to back (a commit between them costs more than an N=64
+                    // MMA) and release the accumulator before the stages.
+                    const uint32_t a = smem_u32(smem + (((L - 1) & 1) ? C::OFF_B1 : C::OFF_B0));
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const uint32_t i = it1 + kb;
+                        if (!mbar_wait_cluster(&full1[i % SMALL_STAGES1], (i / SMALL_STAGES1) & 1)) return false;
+                    }
+                    tc_fence_after();
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const uint32_t b = smem_u32(smem + C::OFF_RING1 + ((it1 + kb) % SMALL_STAGES1) * SMALL_ST1);
+#pragma unroll
+                        for (int k = 0; k < KB / 32; ++k)
+                            mma_i8(d, smem_desc_noswz(a + (kb * 8 + 2 * k) * SMALL_KCHUNK, SMALL_KCHUNK, 128),
+                                   smem_desc_sw128(b + 32 * k), idesc, (kb || k) ? 1u : 0u);
+                    }
+                    mma_commit(acc_full);
+                    for (int kb = 0; kb < nkb; ++kb) mma_commit(&empty1[(it1 + kb) % SMALL_STAGES1]);
+                    it1 += nkb;
+                    ++uu;
+                    small_trace<TRACE>(p, tn, 1, 2, L, step);
+                    return true;
                 }
                 mma_commit(acc_full);
                 ++uu;
@@ -301,7 +358,7 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
         const bool tr = warp == 2 && lane == 0;
         for_each_small_unit(p, [&](int tile, int step, int L) -> bool {
             const int ns = p.out_dim[L] / SMALL_C;
-            const int32_t *bias = bias_s + L * MAX_N + (int)rank * ns;
+            const int32_t *bias = bias_s + L * SMALL_NS;
             const Requant rq = p.rq[L];
             const bool rq_fast = rq.hi_path != 0;
             const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_one = rq.one;
@@ -349,22 +406,55 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty);
+            // This CTA's ns columns of the row: for a hidden layer, K chunks kc0 .. kc0 + 3 of the
+            // next layer's A operand, written into this CTA's buffer and copied from there into
+            // the same place of every other CTA's; for the last layer, 32 logits of the row for
+            // rank 0, staged at [rank][row] (4 KB per CTA) in this CTA's B0 (free at this point).
+            const uint32_t slice_bytes = (uint32_t)(ns / 16) * SMALL_KCHUNK;
+            uint8_t *slice;
             if (!last) {
-                int8_t *dst = p.act_ptr[L & 1] + (size_t)(row0 + r) * MAX_N + (int)rank * ns;
-                st_global_v8(dst, lo);
-                if (ns > 32) st_global_v8(dst + 32, hi);
-                fence_proxy_async_global();          // read next by other CTAs' TMA
-                __syncwarp();
-                if (lane == 0)
-                    for (int c = 0; c < SMALL_C; ++c) mbar_arrive_cluster(map_to_rank(&xbar[xe & 1], (uint32_t)c));
+                const int kc0 = (int)rank * ns / 16;
+                slice = smem + ((L & 1) ? C::OFF_B1 : C::OFF_B0) + kc0 * SMALL_KCHUNK;
+                *reinterpret_cast<uint4 *>(slice + 0 * SMALL_KCHUNK + r * 16) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4 *>(slice + 1 * SMALL_KCHUNK + r * 16) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                if (ns > 32) {
+                    *reinterpret_cast<uint4 *>(slice + 2 * SMALL_KCHUNK + r * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4 *>(slice + 3 * SMALL_KCHUNK + r * 16) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                }
+            } else {
+                slice = smem + C::OFF_B0 + (int)rank * (TM * 32);
+                *reinterpret_cast<uint4 *>(slice + r * 32) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4 *>(slice + r * 32 + 16) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+            }
+            fence_proxy_async_smem();                // read by the copy engine and the tensor core
+            __syncwarp();
+            if (lane == 0) counter_add_release(slice_cnt, 1);
+            if (warp == 2) {
+                // one thread sends the whole slice once every warp's rows are in it (the outcome of
+                // its bounded wait goes to the whole warp, which leaves the walk together)
+                bool ok = true;
+                if (lane == 0) {
+                    ok = counter_wait(slice_cnt, 4 * ue);
+                    if (ok && !last) {
+                        uint64_t *xb = &xbar[xe & 1];
+                        mbar_arrive_expect_tx(xb, (SMALL_C - 1) * slice_bytes);
+                        for (int c = 1; c < SMALL_C; ++c) {
+                            const uint32_t dst = (rank + (uint32_t)c) % SMALL_C;
+                            bulk_copy_to_cluster(map_to_rank(slice, dst), slice, slice_bytes, map_to_rank(xb, dst));
+                        }
+                    } else if (ok && rank == 0) {
+                        mbar_arrive_expect_tx(lbar, (SMALL_C - 1) * (TM * 32));
+                    } else if (ok) {
+                        bulk_copy_to_cluster(map_to_rank(slice, 0), slice, TM * 32, map_to_rank(lbar, 0));
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) return false;
+            }
+            if (tr) small_trace<TRACE>(p, tn2, 2, 2, L, step);
+            if (!last) {
                 ++xe;
-                if (tr) small_trace<TRACE>(p, tn2, 2, 2, L, step);
                 return true;
             }
-            st_global_v8(p.logits + (size_t)(row0 + r) * SC_VOCAB + (int)rank * ns, lo);
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cluster(map_to_rank(lbar, 0));
-            if (tr) small_trace<TRACE>(p, tn2, 2, 2, L, step);
             if (rank != 0) return true;
             // ---- rank 0: the coder step of every row of the tile, from all 256 logits
             if (tr) small_trace<TRACE>(p, tn3, 3, 0, L, step);
@@ -372,29 +462,24 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
             ++lw;
             if (tr) small_trace<TRACE>(p, tn3, 3, 1, L, step);
             int mlogit = -128;
-            {
-                // all sixteen loads in flight at once (L2: the slices come from eight SMs)
-                const uint4 *src = reinterpret_cast<const uint4 *>(p.logits + (size_t)(row0 + r) * SC_VOCAB);
-                uint4 v[16];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) v[i] = __ldcg(src + i);
+            for (int c = 0; c < 8; ++c) {
+                // logits 32c .. 32c + 31 of the row, from CTA c's slice
+                const uint4 a = *reinterpret_cast<const uint4 *>(smem + C::OFF_B0 + c * (TM * 32) + r * 32);
+                const uint4 b = *reinterpret_cast<const uint4 *>(smem + C::OFF_B0 + c * (TM * 32) + r * 32 + 16);
+                const uint32_t w8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint32_t w8[8] = {v[2 * c].x, v[2 * c].y, v[2 * c].z, v[2 * c].w,
-                                            v[2 * c + 1].x, v[2 * c + 1].y, v[2 * c + 1].z, v[2 * c + 1].w};
+                for (int i = 0; i < 8; ++i)
 #pragma unroll
-                    for (int i = 0; i < 8; ++i)
-#pragma unroll
-                        for (int bb = 0; bb < 4; ++bb) mlogit = max(mlogit, pk_get(w8[i], bb));
-                    tmem_st8(taddr + c * 8, w8);
-                }
-                tmem_st_wait();
+                    for (int bb = 0; bb < 4; ++bb) mlogit = max(mlogit, pk_get(w8[i], bb));
+                tmem_st8(taddr + c * 8, w8);
             }
+            tmem_st_wait();
             int amax, sym;
-            RowDivisor d;
+            RowDivisor dv;
             uint32_t fix, cum, f;
-            row_stats<true>(taddr, lut_s, mlogit, d, fix, amax, -1, cum, f);
-            row_find_cached(taddr, lut_s, mlogit, d, fix, amax, dlive ? (uint32_t)dq : 0u, sym, cum, f);
+            row_stats<true>(taddr, lut_s, mlogit, dv, fix, amax, -1, cum, f);
+            row_find_cached(taddr, lut_s, mlogit, dv, fix, amax, dlive ? (uint32_t)dq : 0u, sym, cum, f);
             if (dlive) {
                 DecState s = ds;
                 s.lower += dscale * (uint64_t)cum;
@@ -411,7 +496,7 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
                 // append the token's embedding row to this row's window ring
                 const uint4 *e = reinterpret_cast<const uint4 *>(p.emb + sym * EMB_DIM);
                 uint8_t *dst = reinterpret_cast<uint8_t *>(
-                    p.ering_ptr + (((size_t)(row0 / TM) * WIN + (step & (WIN - 1))) * TM + r) * KB);
+                    p.ering_ptr + (((size_t)ring_block0 + (step & (WIN - 1))) * TM + r) * KB);
                 const uint64_t pol = l2_policy_evict_first();
 #pragma unroll
                 for (int i = 0; i < KB / 32; ++i) {
@@ -434,7 +519,7 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
         }
     }
     // teardown: TMEM is freed only after every MMA issued above has completed; every CTA of the
-    // cluster stays until all remote arrivals are done
+    // cluster stays until all remote arrivals and stores are done
     tc_fence_before();
     __syncthreads();
     if (warp == 1) mbar_wait_cluster_drain(drain, 0);

@@ -673,16 +673,8 @@ static void small_decode(sc_model *m, const int64_t *order, int64_t n_rows, cons
     SC_CUDA(cudaMemcpyAsync(d_steps, steps.data(), sizeof(int32_t) * n_tiles, cudaMemcpyHostToDevice, s));
     ProfScope ps(m->prof, KK_SMALL_DECODE, s, work);
     SmallParams p{};
-    const int64_t rows = (int64_t)clusters * TM;
-    int8_t *a0 = (int8_t *)m->ws_act0.get((size_t)rows * MAX_N, s);
-    int8_t *a1 = (int8_t *)m->ws_act1.get((size_t)rows * MAX_N, s);
-    p.act_ptr[0] = a0;
-    p.act_ptr[1] = a1;
-    p.act[0] = make_tmap(a0, MAX_N, rows, MAX_N, TM);
-    p.act[1] = make_tmap(a1, MAX_N, rows, MAX_N, TM);
-    p.logits = (int8_t *)m->ws_small_logits.get((size_t)rows * SC_VOCAB, s);
     // embedding ring: [clusters][WIN] blocks of 128 rows x 128 B, then the SOS block
-    const int64_t ring_rows = rows * WIN;
+    const int64_t ring_rows = (int64_t)clusters * TM * WIN;
     int8_t *ring = (int8_t *)m->ws_ering.get((size_t)(ring_rows + TM) * KB, s);
     k_sos_block<<<1, TM * KB / 16, 0, s>>>(ring + ring_rows * KB, m->emb);
     SC_LAUNCH_CHECK();
