@@ -519,13 +519,18 @@ __global__ void __launch_bounds__(SMALL_THREADS, 1) k_small_decode(const __grid_
         }
     }
     // teardown: TMEM is freed only after every MMA issued above has completed; every CTA of the
-    // cluster stays until all remote arrivals and stores are done
+    // cluster stays until every thread of the cluster has finished its walk.  In a normal run
+    // every bulk copy into this CTA was waited for (the exchange barriers) before its data was
+    // used; after a timeout (which sets the device error flag before the cluster barrier) a copy
+    // a peer issued before giving up may still be landing here, so the CTA then waits before it
+    // ends.
     tc_fence_before();
     __syncthreads();
     if (warp == 1) mbar_wait_cluster_drain(drain, 0);
     __syncthreads();
     cluster_sync();
     tc_fence_after();
+    if (*(volatile int *)&g_device_error != 0) spin_ns(200000);
     if (warp == 1) tmem_dealloc(tmem_base, SMALL_TMEM_COLS);
 }
 
