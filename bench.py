@@ -104,6 +104,10 @@ def parse_args():
                          "only, int_mm MLP: a few seconds of CPU work per 100 reads)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--mlp-path", default="auto",
+                    choices=["auto", "tcgen05", "tcgen05_small"],
+                    help="decoder to run: auto (the library's choice), tcgen05 (the pair kernel for every "
+                         "batch), tcgen05_small (the small-batch clusters for every batch)")
     ap.add_argument("--no-plugin", action="store_true",
                     help="skip e2e_plugin (the read-level codec interface with host bytes in and out)")
     ap.add_argument("--chunk-len", type=int, default=CHUNK_LEN,
@@ -489,6 +493,8 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
 
     codec = B200Compression(chunk_len=args.chunk_len, gpu=local, model=load_model(name=args.model))
+    if args.mlp_path != "auto":
+        codec.set_mlp_path(args.mlp_path)
     pl = Pipeline(codec, lengths[plan.start:plan.stop], subs, args.chunk_len, args.lsb)
     pl.x[:n_samples].copy_(torch.from_numpy(samples_np))
     # what the round trip must return: the reads themselves, or SigComp's lossy output

@@ -91,6 +91,7 @@ def main(argv=None):
     ap.add_argument("--chunk-len", type=int, default=2048)
     ap.add_argument("--records", type=int, default=400000, help="trace records kept per CTA")
     ap.add_argument("--gpu", type=int, default=0)
+    ap.add_argument("--mlp-path", default="auto", help="decoder to trace (see B200Compression.set_mlp_path)")
     ap.add_argument("--dump", default=None, help="also save the raw records (npz: compress, decode)")
     args = ap.parse_args(argv)
 
@@ -99,6 +100,8 @@ def main(argv=None):
              else make_reads("r10_lognormal", seed=5, count=args.reads))
     L = args.chunk_len
     codec = B200Compression(chunk_len=L, gpu=args.gpu, model=model)
+    if args.mlp_path != "auto":
+        codec.set_mlp_path(args.mlp_path)
     chunks = []
     for sp in codec.split_signals(reads):            # _split_signal on the GPU
         tok = sp[1]
