@@ -726,7 +726,23 @@ def main():
                                                       "split 8 ways + frequency search + range decode)")
         roofline_c = fused_roofline("fused_compress", "k_fused2<0>: fused compress on SM pairs (9 tcgen05 int8 "
                                                       "layers + (cum, freq) selection)")
+        # the signal transform on either side of the codec: HBM-bound byte work, 3 algorithmic bytes
+        # per sample each way (split: 2 B sample in, 1 B token out; reassembly: the reverse; the
+        # large values, about 1 % of deltas, are left out)
+        hbm = None
+        peaks_file = REPO / "MEASURED_PEAKS.json"
+        if peaks_file.exists():
+            hbm = json.loads(peaks_file.read_text()).get("hbm_gbs")
+        signal = {}
+        for kind in ("split", "reassemble"):
+            ms, n, samples = prof.get(kind, (0.0, 0, 0))
+            if ms > 0 and n:
+                gbs = 3 * samples / (ms * 1e-3) / 1e9
+                signal[kind] = {"launch_ms": round(ms / n, 3), "samples_per_launch": int(samples / n),
+                                "achieved_gbs": round(gbs, 1),
+                                "frac_of_hbm": round(gbs / hbm, 4) if hbm else None}
         if roofline is not None:
+            roofline["signal_kernels"] = signal or None
             roofline["kernel_ms"] = {k: round(v[0], 2) for k, v in prof.items()}
             roofline["kernel_launches"] = {k: v[1] for k, v in prof.items()}
 

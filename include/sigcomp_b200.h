@@ -290,7 +290,8 @@ SC_API int sc_mlp_logits_device_noalloc(sc_model *model, const int16_t *windows,
  * layer, 4 frequency/symbol selection, 5 range encoder, 6 stream compaction,
  * 7 decoder step, 8 fused compress kernel (all layers + selection; work = rows),
  * 9 fused persistent decoder on SM pairs (work = decoded tokens), 10 small-batch
- * decoder on clusters of eight SMs (work = decoded tokens).
+ * decoder on clusters of eight SMs (work = decoded tokens), 11 signal split and
+ * 12 signal reassembly (work = samples).
  */
 SC_API int sc_profile_enable(sc_model *model, int32_t enable);
 SC_API int sc_profile_read(sc_model *model, int32_t kind, double *total_ms, int64_t *launches, int64_t *work);

@@ -28,7 +28,7 @@ EXPORTS = (
 )
 
 KERNEL_KINDS = ("windows", "layer0", "hidden", "last_layer", "cdf_select", "encode", "compact", "decode_step",
-                "fused_compress", "fused_decode", "small_decode")
+                "fused_compress", "fused_decode", "small_decode", "split", "reassemble")
 
 _lib = None
 

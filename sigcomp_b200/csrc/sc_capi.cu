@@ -39,7 +39,8 @@ int encode_logits_device(sc_model *m, const int8_t *logits, const uint8_t *symbo
                          int64_t *word_offsets, uint8_t *errors_d, cudaStream_t s);
 void decode_logits_device(sc_model *m, const int8_t *logits, const int64_t *off_d, int64_t n, const uint32_t *words,
                           const int64_t *word_offsets, uint8_t *symbols, uint8_t *errors_d, cudaStream_t s);
-int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *off_d, int64_t n_reads, int lsb,
+int reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t *off_d, const int64_t *off_h,
+                             int64_t n_reads, int lsb,
                              const uint8_t *small, const int64_t *small_off, const uint16_t *large,
                              const uint32_t *large_pos, const int64_t *large_off, int16_t *samples,
                              cudaStream_t s);
@@ -601,7 +602,8 @@ int sc_reassemble_signal_device(sc_model *m, const int16_t *sig0, const int64_t 
         SC_CUDA(cudaStreamSynchronize(s));
         int rc = check_read_offsets(off_h.data(), n_reads);
         if (rc) return rc;
-        if (reassemble_signal_device(m, sig0, sample_offsets, n_reads, lsb, tokens, token_offsets, large, large_pos,
+        if (reassemble_signal_device(m, sig0, sample_offsets, off_h.data(), n_reads, lsb, tokens, token_offsets,
+                                     large, large_pos,
                                      large_offsets, samples, s)) {
             set_error("token and large-value streams do not match the read lengths");
             return SC_ERR_INVALID_ARGUMENT;

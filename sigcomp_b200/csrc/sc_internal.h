@@ -60,7 +60,7 @@ struct DevBuf {
 enum KernelKind {
     KK_WINDOWS = 0, KK_LAYER0 = 1, KK_HIDDEN = 2, KK_LAST = 3, KK_CDF = 4, KK_ENCODE = 5,
     KK_COMPACT = 6, KK_DECODE = 7, KK_FUSED_COMPRESS = 8, KK_FUSED_DECODE = 9, KK_SMALL_DECODE = 10,
-    KK_KINDS = 11
+    KK_SPLIT = 11, KK_REASSEMBLE = 12, KK_KINDS = 13
 };
 
 // CUDA-event timing of individual launches on their own stream.  Disabled by
