@@ -94,7 +94,10 @@ template <bool DECODE>
 struct F2Cfg {
     // decode: layer 0 is one pass over K for both 256-column halves (two accumulators),
     // so a stage holds the ring block and both weight halves: the block is read from
-    // the ring once per step instead of twice
+    // the ring once per step instead of twice.  The two halves of the other 512-wide
+    // layers share their stages the same way, one unit after the other: a stage holds a
+    // K block of the activations and of both weight halves, half 0 keeps it and half 1
+    // releases it, so each activation K block is loaded once per layer, not twice.
     static constexpr int STAGES = 4;
     static constexpr int STAGE_BYTES = A_BYTES + (DECODE ? 2 : 1) * B_HALF;   // 48 KB / 32 KB
     static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 192 KB / 128 KB
@@ -382,8 +385,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             // the weights and activations that live in L2
             const uint64_t ring_policy = l2_policy_evict_first();
             for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
-                if (DECODE && L == 0 && nh == 1) return true;       // loaded with half 0
+                // decode: half 1 of a layer is loaded with half 0 (layer 0: one dual pass; the
+                // other layers: the two halves share their activation K blocks)
                 const int nkb = p.in_dim[L] / KB;
+                if (DECODE && nh == 1 && (L == 0 || nkb <= C::STAGES)) return true;
                 trace_ev<TRACE>(p, tn, 0, 0, L, nh, tt, gs);
                 if (nh == 0 && (L >= 1 || (DECODE && step > 0))) {
                     // layer L-1 of this tile is written (decode layer 0: the previous step's
@@ -402,13 +407,15 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     uint8_t *st = smem + s * C::STAGE_BYTES;
                     const uint32_t fb = map_to_rank(&full[s], 0);
                     const bool a_tma = DECODE || L != 0;
-                    const bool dual = DECODE && L == 0;
+                    // decode: layer 0 and the two-half layers load both weight halves per K block
+                    const bool both = DECODE && (L == 0 || (p.out_dim[L] == 2 * TN && nkb <= C::STAGES));
                     if (rank == 0)
-                        mbar_arrive_expect_tx(&full[s], 2 * ((dual ? 2 : 1) * B_HALF + (a_tma ? A_BYTES : B_HALF)));
+                        mbar_arrive_expect_tx(&full[s], 2 * ((both ? 2 : 1) * B_HALF + (a_tma ? A_BYTES : B_HALF)));
                     if (kstep == 2) {
                         tma_load_2d_pair(st, &p.w[L], fb, (kb + 1) * KB, nh * TN + (int)rank * (TN / 2));
                     } else if (L != 0) {
                         tma_load_2d_pair(st, &p.act[(L - 1) & 1], fb, kb * KB, slot_row0 + tt * TM);
+                        if (both) tma_load_2d_pair(st + A_BYTES + B_HALF, &p.w[L], fb, kb * KB, TN + (int)rank * (TN / 2));
                     } else if (DECODE) {
                         // window position kb holds token step - 64 + kb (start-of-sequence before 0)
                         const int tau = step - WIN + kb;
@@ -441,12 +448,17 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         if (lane == 0 && rank == 0) {
             // ---- MMA issuer (leader CTA only)
             uint32_t it = 0, uu = 0, li = 0;
+            uint32_t it_shared = 0;                    // decode: first stage of the current two-half layer
             unsigned int tn = 0;                       // trace records written
             for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
                 // decoding layer 0: half 1 accumulates in the other buffer during half 0's pass
                 if (DECODE && L == 0 && nh == 1) return true;
                 const bool dual = DECODE && L == 0;
                 const int nkb = p.in_dim[L] / KB;
+                // decoding a two-half layer >= 1: half 0 reads each stage after its wait and keeps
+                // it; half 1 reads the same stages again (its own weight half) and releases them
+                const bool sh = DECODE && L != 0 && p.out_dim[L] == 2 * TN && nkb <= C::STAGES;
+                const bool shared0 = sh && nh == 0, shared1 = sh && nh == 1;
                 const int ab = uu & 1;
                 trace_ev<TRACE>(p, tn, 1, 0, L, nh, tt, gs);
                 if (!mbar_wait_cluster(&acc_empty[ab], ((uu >> 1) & 1) ^ 1)) return false;
@@ -457,12 +469,25 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 tc_fence_after();
                 const uint32_t d = tmem_base + ab * TN;
                 const int kstep = (!DECODE && L == 0) ? 2 : 1;
-                for (int kb = 0; kb < nkb; kb += kstep, ++it) {
+                if (shared0) it_shared = it;
+                if (shared1) {
+                    for (int kb = 0; kb < nkb; ++kb) {
+                        const int s = (it_shared + kb) % C::STAGES;
+                        const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+                        mma_k_block_pair(d, st, st + A_BYTES + B_HALF, kb == 0);
+                        mma_commit_pair(&empty[s], 0x3);
+                    }
+                }
+                for (int kb = 0; kb < nkb && !shared1; kb += kstep, ++it) {
                     const int s = it % C::STAGES;
                     if (!mbar_wait_cluster(&full[s], (it / C::STAGES) & 1)) return false;
                     if (L == 0 && kb < 4) trace_ev<TRACE>(p, tn, 1, 3, L, kb, tt, gs);
                     tc_fence_after();
                     const uint32_t st = smem_u32(smem + s * C::STAGE_BYTES);
+                    if (shared0) {
+                        mma_k_block_pair(d, st, st + A_BYTES, kb == 0);
+                        continue;                          // the stage stays for half 1
+                    }
                     if (kstep == 2) {
                         const uint32_t g = smem_u32(xbuf + gb * G_BYTES);
                         mma_k_block_pair(d, g + kb * KB, st + A_BYTES, kb == 0);

@@ -15,6 +15,11 @@ wait here asserts that, so an ordering that lets a waiter fall two phases behind
 instead of corrupting a run on the GPU.  The model also checks that no barrier ever receives more
 arrivals than its count, and that every role finishes (no deadlock).
 
+In the decoder, the two 256-column halves of each layer between the first and the last share their
+stages: the producer loads a K block's activations and both weight halves once (with half 0), the
+MMA issuer's half 0 waits for each stage and keeps it, and half 1 reads the same stages again and
+releases them.
+
 The decoder's unit walk is the kernel's one-launch schedule: each of six lanes runs a queue of
 pair-tiles back to back (longest first, to the least-loaded lane), cut into segments at every
 step where a lane changes tile, as `build_decode_schedule` in sc_mlp_tc.cu does for one pair.
@@ -187,8 +192,8 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
         issued = []                                   # per K block: (first buffer, its K block number, its fill number)
         try:
             for gs, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
-                if decode and L == 0 and nh == 1:
-                    continue                          # loaded with half 0
+                if decode and nh == 1 and (L == 0 or not slots):
+                    continue                          # loaded with half 0 (shared stages)
                 nkb = in_dim[L] // KB
                 if nh == 0 and (L >= 1 or (decode and step > 0)):
                     k = gs * NL + L - 1
@@ -209,8 +214,10 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
                         uses[j] += 1
                     s = bufs[0]
                     dual = decode and L == 0
+                    # decode without slots: the two halves of a layer >= 1 share each stage
+                    both = dual or (decode and not slots and L < NL - 1)
                     a_tma = decode or L != 0
-                    nbytes = 2 * ((2 if dual else 1) * 16 + (16 if a_tma else 16))
+                    nbytes = 2 * ((2 if both else 1) * 16 + (16 if a_tma else 16))
                     if rank == 0:
                         full[s].expect_tx(nbytes)
                         full[s].arrive()
@@ -240,6 +247,7 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
 
     def mma():
         it = uu = li = pos = 0
+        it_shared = 0                                 # first stage of the current shared layer
         firsts = [0] * nbuf                           # per buffer: K blocks it has led so far
         try:
             for gs, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
@@ -255,14 +263,26 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
                 if not decode and L == 0 and nh == 0:
                     yield from pwait("mma", g_full[gb], (li >> 1) & 1, (li >> 1) + 1)
                 kstep = 2 if (not decode and L == 0) else 1
-                for kb in range(0, nkb, kstep):
+                # decode without slots, layers 0 < L < NL-1: half 0 waits for each stage and keeps
+                # it, half 1 reads the same stages again and releases them
+                sh = decode and not slots and 0 < L < NL - 1
+                if sh and nh == 0:
+                    it_shared = it
+                if sh and nh == 1:
+                    n_ring = nbuf - 1 if plant == "stages" else nbuf
+                    for kb in range(nkb):
+                        j = (it_shared + kb) % n_ring
+                        commits.append([empty[0][j], empty[1][j]])
+                        yield
+                for kb in range(0, nkb if not (sh and nh == 1) else 0, kstep):
                     bufs, adv = kblock_bufs(L, pos, it, nbuf - 1 if plant == "stages" else nbuf)
                     s = bufs[0]
                     f = firsts[s]
                     yield from pwait("mma", full[s], f & 1, f + 1)
                     firsts[s] += 1
-                    for j in bufs:                    # one commit per buffer, in order
-                        commits.append([empty[0][j], empty[1][j]])
+                    if not (sh and nh == 0):
+                        for j in bufs:                # one commit per buffer, in order
+                            commits.append([empty[0][j], empty[1][j]])
                     it += 1
                     pos += adv
                     yield
