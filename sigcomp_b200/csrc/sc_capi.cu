@@ -232,6 +232,13 @@ int sc_model_create(int device, int32_t window, int32_t emb_dim, int32_t num_lay
             SC_CUDA(cudaMemcpy(L.w, weights[l], wb, cudaMemcpyHostToDevice));
             SC_CUDA(cudaMalloc(&L.bias, sizeof(int32_t) * L.out_dim));
             SC_CUDA(cudaMemcpy(L.bias, biases[l], sizeof(int32_t) * L.out_dim, cudaMemcpyHostToDevice));
+            // the pair decoder adds the bias of layers >= 1 with an MMA (fast requantisation only)
+            const std::vector<int8_t> bt = l > 0 && L.rq.hi_path ? bias_tile(biases[l], L.out_dim)
+                                                                   : std::vector<int8_t>();
+            if (!bt.empty()) {
+                SC_CUDA(cudaMalloc(&L.bdig, bt.size()));
+                SC_CUDA(cudaMemcpy(L.bdig, bt.data(), bt.size(), cudaMemcpyHostToDevice));
+            }
         }
         m->tc_ok = mlp_tc_supported(m.get());
         if (m->tc_ok) mlp_tc_prepare(m.get());
@@ -260,6 +267,7 @@ int sc_model_destroy(sc_model *m)
             cudaFree(L.w);
             cudaFree(L.w_tc);
             cudaFree(L.bias);
+            cudaFree(L.bdig);
         }
         for (DevBuf *b : {&m->ws_windows, &m->ws_act0, &m->ws_act1, &m->ws_logits, &m->ws_pairs, &m->ws_stage,
                           &m->ws_nwords, &m->ws_err, &m->ws_scan, &m->ws_tmp, &m->ws_order, &m->ws_state,

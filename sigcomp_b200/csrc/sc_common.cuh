@@ -90,6 +90,15 @@ __device__ __forceinline__ uint32_t requant4_hi(const uint32_t *acc, int4 bias, 
     return d & ~(sgn & relu_mask);
 }
 
+// requant4_hi for an accumulator that already holds the bias (no bias load, no bias add)
+__device__ __forceinline__ uint32_t requant4_hi_nb(const uint32_t *acc, int32_t m0, int32_t hs, uint32_t relu_mask) {
+    const uint32_t d = sat_pack4(__mulhi((int32_t)acc[0], m0) >> hs, __mulhi((int32_t)acc[1], m0) >> hs,
+                                 __mulhi((int32_t)acc[2], m0) >> hs, __mulhi((int32_t)acc[3], m0) >> hs);
+    uint32_t sgn;
+    asm("prmt.b32 %0, %1, %1, 0xBA98;" : "=r"(sgn) : "r"(d));
+    return d & ~(sgn & relu_mask);
+}
+
 __device__ __forceinline__ uint32_t requant4(const uint32_t *acc, int4 bias, const Requant &q) {
     if (q.hi_path) {
         const int32_t m0 = (int32_t)q.m0, hs = q.hi_shift, lo = q.lo;

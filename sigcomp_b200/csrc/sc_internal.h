@@ -134,8 +134,16 @@ struct LayerDev {
     int8_t *w = nullptr;        // [out][in] row-major (CUDA-core path)
     int8_t *w_tc = nullptr;     // tensor-core operand layout (tcgen05 path), or null
     int32_t *bias = nullptr;    // [out]
+    // bias tile of the pair decoder, [256][128] int8 (null when the bias stays in the epilogue):
+    // row n holds, for each 256-column half h, 32 int8 digits of bias[h * 256 + n] in bytes
+    // 64h .. 64h + 31 and the multipliers 16 x 127, 16 x 1 in bytes 64h + 32 .. 64h + 63
+    int8_t *bdig = nullptr;
     Requant rq;
 };
+
+// Bias tile of one layer (see LayerDev::bdig), or an empty vector when the layer cannot use one:
+// a width other than 256 or 512, or a bias outside the range the digits reach (|b| <= 258,127).
+std::vector<int8_t> bias_tile(const int32_t *bias, int out_dim);
 
 // Launch the CUDA-core MLP: windows int16 [rows][window] -> logits int8 [rows][256].
 void mlp_simple(sc_model *m, const int16_t *windows, int64_t rows, int8_t *logits, cudaStream_t s);
@@ -195,6 +203,7 @@ struct sc_model {
     std::vector<sc::LayerDev> layers;
     std::vector<CUtensorMap> tc_wmaps;   // weight tensor maps of the tcgen05 path (box 256 rows)
     std::vector<CUtensorMap> tc_wmaps2;  // weight tensor maps for CTA pairs (box 128 rows)
+    std::vector<CUtensorMap> tc_bmaps2;  // bias tile maps for CTA pairs (box 128 rows; unset without a tile)
     std::vector<CUtensorMap> small_wmaps;  // small-batch decoder: box out_dim / 8 rows
     sc::Profiler prof;
     // unit trace of the first SM pair of the fused kernels (sc_trace_enable)

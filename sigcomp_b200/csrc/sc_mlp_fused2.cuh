@@ -21,8 +21,13 @@
 //     one 128-row x 128-byte block per window position); the last-layer
 //     epilogue appends each decoded token's embedding row, so a step writes
 //     one block per tile instead of building all 64.
+//   - decode: the layers after the first add their bias with one K = 32 MMA
+//     against a resident bias tile (loaded once per layer and step), so their
+//     epilogues requantise without loading or adding a bias.
 // No TMA load uses cluster multicast.
 #pragma once
+
+#include <type_traits>
 
 namespace sc {
 
@@ -43,6 +48,13 @@ struct DecSeg {
 
 struct Fused2Params {
     CUtensorMap w[FMAX_LAYERS];       // weights, box 128 rows x 128 B (half of a 256-row unit)
+    // decode: bias tiles of layers >= 1 (box 128 rows x 128 B, one per CTA of the pair).  Row i
+    // of CTA r's tile serves output column h * 256 + r * 128 + i of half h: bytes 64h .. 64h + 31
+    // hold 32 int8 digits of that column's bias and bytes 64h + 32 .. 64h + 63 the constants
+    // 16 x 127, 16 x 1.  One K = 32 MMA with the constants as A (the same in every row) and the
+    // digits as B puts the bias into the accumulator before the layer's K blocks.
+    CUtensorMap bt[FMAX_LAYERS];
+    uint32_t bias_mma;                // bit L: layer L's bias enters through its bias tile
     CUtensorMap act[2];               // activation ping-pong, box 128 x 128 B
     int8_t *act_ptr[2];
     const int32_t *bias[FMAX_LAYERS];
@@ -102,10 +114,14 @@ struct F2Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + (DECODE ? 2 : 1) * B_HALF;   // 48 KB / 32 KB
     static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 192 KB / 128 KB
     static constexpr int X_BYTES = DECODE ? 0 : 2 * G_BYTES;
-    static constexpr int OFF_BIAS = OFF_X + X_BYTES;
-    static constexpr int OFF_LUT = OFF_BIAS + BIAS_MAX * 4;
+    // decode: the current layer's bias tile (16 KB); its SMEM bias table holds layer 0 only
+    static constexpr int OFF_BT = OFF_X + X_BYTES;
+    static constexpr int BT_BYTES = DECODE ? TM * KB : 0;
+    static constexpr int OFF_BIAS = OFF_BT + BT_BYTES;
+    static constexpr int BIAS_ENTRIES = DECODE ? MAX_N : BIAS_MAX;
+    static constexpr int OFF_LUT = OFF_BIAS + BIAS_ENTRIES * 4;
     static constexpr int OFF_BAR = OFF_LUT + 256 * 8;
-    static constexpr int NBAR = 2 * STAGES + 9;     // ... + the teardown drain barrier
+    static constexpr int NBAR = 2 * STAGES + 11;    // ... + the teardown drain barrier + bias tile pair
     static constexpr int OFF_CNT = OFF_BAR + NBAR * 8;
     static constexpr int OFF_TMEM = OFF_CNT + 8 * 4;
     static constexpr int SMEM = OFF_TMEM + 16 + 1024;
@@ -268,8 +284,9 @@ __device__ __forceinline__ void row_find_cached(uint32_t taddr, const uint64_t *
 }
 
 // Walk this pair's units in the fixed order both CTAs and every role follow, calling
-// f(gs, tt, pt, step, L, nh) for each unit: layer L, output half nh, of pair-tile pt in slot tt
+// f(gs, tt, pt, step, L, nh, fl) for each unit: layer L, output half nh, of pair-tile pt in slot tt
 // at that tile's step `step`.  Pair-tile pt covers tiles 2*pt (rank 0) and 2*pt+1 (rank 1).
+// fl bit 0: the first unit of layer L in this step (or group), bit 1: the last.
 //   decode: gs is the pair's global step; every slot's lane runs its pair-tiles back to back,
 //           so slot tt's units of global step gs are its (gs * NL + L)-th layer completion
 //   compress: gs is the group of up to kt2() tiles; every tile takes one step
@@ -283,6 +300,12 @@ __device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
         for (int sg = p.pair_seg[pair]; sg < p.pair_seg[pair + 1]; ++sg) {
             const DecSeg *S = p.segs + sg;
             const int s1 = S->s1;
+            int first_tt = KT2, last_tt = -1;      // the segment's first and last busy lanes
+            for (int tt = 0; tt < KT2; ++tt)
+                if (S->pt[tt] >= 0) {
+                    first_tt = min(first_tt, tt);
+                    last_tt = tt;
+                }
             for (int gs = S->s0; gs < s1; ++gs)
                 for (int L = 0; L < NL; ++L)
 #pragma unroll 1
@@ -291,8 +314,10 @@ __device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
                         if (pt < 0) continue;
                         const int step = gs - S->start[tt];
                         const int NH = p.out_dim[L] / TN;
-                        for (int nh = 0; nh < NH; ++nh)
-                            if (!f(gs, tt, pt, step, L, nh)) return;
+                        for (int nh = 0; nh < NH; ++nh) {
+                            const int fl = (tt == first_tt && nh == 0 ? 1 : 0) | (tt == last_tt && nh == NH - 1 ? 2 : 0);
+                            if (!f(gs, tt, pt, step, L, nh, fl)) return;
+                        }
                     }
         }
         return;
@@ -307,8 +332,10 @@ __device__ __forceinline__ void for_each_unit2(const Fused2Params &p, F &&f)
             for (int tt = 0; tt < gn; ++tt) {
                 const int pt = pair + (g0 + tt) * NP;
                 const int NH = p.out_dim[L] / TN;
-                for (int nh = 0; nh < NH; ++nh)
-                    if (!f(grp, tt, pt, 0, L, nh)) return;
+                for (int nh = 0; nh < NH; ++nh) {
+                    const int fl = (tt == 0 && nh == 0 ? 1 : 0) | (tt == gn - 1 && nh == NH - 1 ? 2 : 0);
+                    if (!f(grp, tt, pt, 0, L, nh, fl)) return;
+                }
             }
     }
 }
@@ -335,6 +362,9 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
     uint64_t *g_full = acc_empty + 2, *g_empty = g_full + 2;
     // drain: the MMA issuer's last commit (both CTAs); TMEM is freed only after it
     uint64_t *drain = g_empty + 2;
+    // decode: bias tile loaded (leader: expect-tx + both CTAs' bytes) / free again (MMA commit)
+    uint64_t *bt_full = drain + 1, *bt_empty = drain + 2;
+    uint8_t *btile = smem + C::OFF_BT;
     // act_cnt[tt]: +1 per epilogue warp of this CTA when its tile of slot tt finishes a
     // layer; completion number k is reached at act_cnt[tt] >= EPI_WARPS * (k + 1)
     uint32_t *act_cnt = (uint32_t *)(smem + C::OFF_CNT);
@@ -358,6 +388,8 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             mbar_init(&g_empty[b], 1);
         }
         mbar_init(drain, 1);
+        mbar_init(bt_full, 1);
+        mbar_init(bt_empty, 1);
         for (int tt = 0; tt < 8; ++tt) act_cnt[tt] = 0;
         fence_mbar_init();
     }
@@ -366,7 +398,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         tmem_relinquish_pair();
     }
     for (int i = threadIdx.x; i < SC_VOCAB; i += blockDim.x) lut_s[i] = p.lut[i];
-    for (int l = 0; l < NL; ++l)
+    for (int l = 0; l < (DECODE ? 1 : NL); ++l)
         for (int i = threadIdx.x; i < p.out_dim[l]; i += blockDim.x) bias_s[l * MAX_N + i] = p.bias[l][i];
     tc_fence_before();
     __syncthreads();
@@ -379,12 +411,13 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         if (lane == 0) {
             // ---- TMA producer (both CTAs): own activation rows + own half of the weights
             uint32_t it = 0;
+            uint32_t nbt = 0;                          // bias tiles loaded
             unsigned int tn = 0;                       // trace records written
             bool aborted = false;
             // the embedding ring (hundreds of MB) streams from DRAM: keep it from evicting
             // the weights and activations that live in L2
             const uint64_t ring_policy = l2_policy_evict_first();
-            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
+            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh, int fl) -> bool {
                 // decode: half 1 of a layer is loaded with half 0 (layer 0: one dual pass; the
                 // other layers: the two halves share their activation K blocks)
                 const int nkb = p.in_dim[L] / KB;
@@ -425,6 +458,14 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
+                if (DECODE && L != 0 && (fl & 1) && ((p.bias_mma >> L) & 1u)) {
+                    // the layer's bias tile, once per layer and step, after the first unit's K
+                    // blocks and once the previous layer's last bias MMA has read the buffer
+                    if (!mbar_wait_cluster(bt_empty, (nbt & 1) ^ 1)) return !(aborted = true);
+                    if (rank == 0) mbar_arrive_expect_tx(bt_full, 2 * C::BT_BYTES);
+                    tma_load_2d_pair(btile, &p.bt[L], map_to_rank(bt_full, 0), 0, (int)rank * TM);
+                    ++nbt;
+                }
                 trace_ev<TRACE>(p, tn, 0, 2, L, nh, tt, gs);
                 return true;
             });
@@ -441,6 +482,11 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     if (rank == 0) mbar_wait_cluster_drain(&full[s], ph);
                     else mbar_wait_cluster_drain(&empty[s], ph);
                 }
+                // the last bias tile, the same way
+                if (DECODE && nbt > 0) {
+                    if (rank == 0) mbar_wait_cluster_drain(bt_full, (nbt - 1) & 1);
+                    else mbar_wait_cluster_drain(bt_empty, (nbt - 1) & 1);
+                }
                 spin_ns(100000);
             }
         }
@@ -449,8 +495,9 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             // ---- MMA issuer (leader CTA only)
             uint32_t it = 0, uu = 0, li = 0;
             uint32_t it_shared = 0;                    // decode: first stage of the current two-half layer
+            uint32_t nbt = 0;                          // bias tiles used
             unsigned int tn = 0;                       // trace records written
-            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
+            for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh, int fl) -> bool {
                 // decoding layer 0: half 1 accumulates in the other buffer during half 0's pass
                 if (DECODE && L == 0 && nh == 1) return true;
                 const bool dual = DECODE && L == 0;
@@ -469,6 +516,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 tc_fence_after();
                 const uint32_t d = tmem_base + ab * TN;
                 const int kstep = (!DECODE && L == 0) ? 2 : 1;
+                // decode, bias tile: after the K blocks one K = 32 MMA adds the bias to the
+                // accumulator (integer sums: the order does not matter), so the tile has the
+                // unit's K blocks to arrive; it is released after the layer's last bias MMA
+                const bool bmma = DECODE && L != 0 && ((p.bias_mma >> L) & 1u);
                 if (shared0) it_shared = it;
                 if (shared1) {
                     for (int kb = 0; kb < nkb; ++kb) {
@@ -498,6 +549,13 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     }
                     mma_commit_pair(&empty[s], 0x3);
                 }
+                if (bmma) {
+                    if ((fl & 1) && !mbar_wait_cluster(bt_full, (nbt++) & 1)) return false;
+                    tc_fence_after();
+                    const uint32_t b0 = smem_u32(btile) + 64 * nh;
+                    mma_i8_pair(d, smem_desc_sw128(b0 + 32), smem_desc_sw128(b0), idesc_i8(2 * TM, TN), 1u);
+                    if (fl & 2) mma_commit_pair(bt_empty, 0x3);
+                }
                 mma_commit_pair(&acc_full[ab], 0x3);
                 if (dual) mma_commit_pair(&acc_full[ab ^ 1], 0x3);
                 trace_ev<TRACE>(p, tn, 1, 2, L, nh, tt, gs);
@@ -524,7 +582,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         const int part = (warp - 2) >> 2;
         const int r = q * 32 + lane;
         uint32_t uu = 0, lu = 0;
-        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
+        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh, int fl) -> bool {
             const int ab = uu & 1;
             const bool tr = warp == 2 && lane == 0;
             if (tr) trace_ev_atomic<TRACE>(p, 2, 0, L, nh, tt, gs);
@@ -572,22 +630,32 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             const bool rq_fast = rq.hi_path != 0;
             const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_one = rq.one;
             const uint32_t rq_relu = rq.lo == 0 ? 0xFFFFFFFFu : 0u;
-            const int32_t *bias = bias_s + L * MAX_N;
+            // decode keeps only layer 0's bias in SMEM; the other layers' biases enter through
+            // their bias tiles (nb), or are read from global memory when a layer has none
+            const int32_t *bias = (!DECODE || L == 0) ? bias_s + L * MAX_N : p.bias[L];
+            const bool nb = DECODE && L != 0 && ((p.bias_mma >> L) & 1u);
             const uint32_t acc_empty_leader = map_to_rank(&acc_empty[ab], 0);
             const int tile = 2 * pt + (int)rank;
-            if (L < NL - 1) {
+            // hidden layers; NB: the accumulator holds the bias already (decode, bias tile).  The
+            // two forms are separate instantiations, so neither carries the other's registers.
+            auto hidden_unit = [&](auto NB) -> bool {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;
                 // requantise chunk c (32 columns) of this row and store it to the activations
                 // with one 32-byte store
                 auto store_chunk = [&](const uint32_t (&va)[32], int c) {
-                    const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
                     uint32_t packed[8];
-                    if (rq_fast) {
+                    if constexpr (decltype(NB)::value) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one);
+                        for (int i = 0; i < 8; ++i) packed[i] = requant4_hi_nb(&va[4 * i], rq_m0, rq_hs, rq_relu);
                     } else {
+                        const int4 *bv = reinterpret_cast<const int4 *>(bias + nh * TN + c * 32);
+                        if (rq_fast) {
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
+                            for (int i = 0; i < 8; ++i) packed[i] = requant4_hi(&va[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one);
+                        } else {
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) packed[i] = requant4(&va[4 * i], bv[i], rq);
+                        }
                     }
                     st_global_v8(dst_row + c * 32, packed);
                 };
@@ -619,6 +687,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 }
                 if (tr) trace_ev_atomic<TRACE>(p, 2, 2, L, nh, tt, gs);
                 return true;
+            };
+            if (L < NL - 1) {
+                if (nb) return hidden_unit(std::true_type{});
+                return hidden_unit(std::false_type{});
             }
             if (mine) {
                 // last layer: requantise the 256 logits of this row, keep them packed in the
@@ -633,7 +705,9 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     uint32_t w8[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
-                        w8[i] = rq_fast ? requant4_hi(&v[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one) : requant4(&v[4 * i], bv[i], rq);
+                        w8[i] = nb ? requant4_hi_nb(&v[4 * i], rq_m0, rq_hs, rq_relu)
+                                   : rq_fast ? requant4_hi(&v[4 * i], bv[i], rq_m0, rq_hs, rq_relu, rq_one)
+                                             : requant4(&v[4 * i], bv[i], rq);
 #pragma unroll
                         for (int b = 0; b < 4; ++b) mlogit = max(mlogit, pk_get(w8[i], b));
                     }
@@ -704,7 +778,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
         const int tw = threadIdx.x - 32 * (2 + EPI_WARPS);   // 0..63
         const int j = tw & 7, r0 = tw >> 3;
         uint32_t li = 0;
-        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh) -> bool {
+        for_each_unit2<DECODE>(p, [&](int gs, int tt, int pt, int step, int L, int nh, int fl) -> bool {
             if (L != 0 || nh != 0) return true;
             const int gb = li & 1;
             if (!__all_sync(0xffffffffu, mbar_wait_cluster(&g_empty[gb], ((li >> 1) & 1) ^ 1))) return false;

@@ -377,6 +377,33 @@ CUtensorMap make_tmap(const void *base, uint64_t cols, uint64_t rows, uint64_t p
 
 }  // namespace
 
+std::vector<int8_t> bias_tile(const int32_t *bias, int out_dim)
+{
+    if (out_dim != TN && out_dim != 2 * TN) return {};
+    // bias[c] = 127 * (d_0 + ... + d_15) + d_16 with every digit in [-127, 127] and |d_16| <= 63
+    std::vector<int8_t> t((size_t)TN * KB, 0);
+    for (int n = 0; n < TN; ++n) {
+        int8_t *row = t.data() + (size_t)n * KB;
+        for (int h = 0; h < 2; ++h) {
+            int8_t *q = row + 64 * h;
+            for (int j = 32; j < 48; ++j) q[j] = 127;
+            for (int j = 48; j < 64; ++j) q[j] = 1;
+            if (h * TN >= out_dim) continue;
+            const int64_t b = bias[h * TN + n];
+            int64_t hi = b >= 0 ? (b + 63) / 127 : -((-b + 63) / 127);
+            const int64_t lo = b - 127 * hi;
+            if (hi > 16 * 127 || hi < -16 * 127) return {};
+            for (int j = 0; j < 16; ++j) {
+                const int64_t d = hi > 127 ? 127 : (hi < -127 ? -127 : hi);
+                q[j] = (int8_t)d;
+                hi -= d;
+            }
+            q[16] = (int8_t)lo;
+        }
+    }
+    return t;
+}
+
 bool mlp_tc_supported(const sc_model *m)
 {
     if (m->emb_dim != EMB_DIM || m->window != WIN || m->layers[0].in_dim != WIN * EMB_DIM) return false;
@@ -407,6 +434,10 @@ void mlp_tc_prepare(sc_model *m)
     auto &maps2 = m->tc_wmaps2;
     maps2.clear();
     for (auto &L : m->layers) maps2.push_back(make_tmap(L.w, L.in_dim, L.out_dim, L.in_dim, TN / 2));
+    auto &bmaps = m->tc_bmaps2;
+    bmaps.assign(m->layers.size(), CUtensorMap{});
+    for (size_t l = 0; l < m->layers.size(); ++l)
+        if (m->layers[l].bdig) bmaps[l] = make_tmap(m->layers[l].bdig, KB, TN, KB, TN / 2);
     SC_CUDA(cudaFuncSetAttribute(k_fused<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FCfg<false>::SMEM));
     SC_CUDA(cudaFuncSetAttribute(k_small_decode<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallCfg::SMEM));
     SC_CUDA(cudaFuncSetAttribute(k_small_decode<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SmallCfg::SMEM));
@@ -511,8 +542,13 @@ static void fused2_common(sc_model *m, Fused2Params &p, int grid, cudaStream_t s
     p.act[0] = make_tmap(a0, MAX_N, rows, MAX_N, TM);
     p.act[1] = make_tmap(a1, MAX_N, rows, MAX_N, TM);
     p.num_layers = m->num_layers;
+    p.bias_mma = 0;
     for (int l = 0; l < m->num_layers; ++l) {
         p.w[l] = m->tc_wmaps2[l];
+        if (m->layers[l].bdig) {
+            p.bt[l] = m->tc_bmaps2[l];
+            p.bias_mma |= 1u << l;
+        }
         p.bias[l] = m->layers[l].bias;
         p.rq[l] = m->layers[l].rq;
         p.in_dim[l] = m->layers[l].in_dim;

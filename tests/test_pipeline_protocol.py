@@ -20,6 +20,12 @@ stages: the producer loads a K block's activations and both weight halves once (
 MMA issuer's half 0 waits for each stage and keeps it, and half 1 reads the same stages again and
 releases them.
 
+The decoder's layers after the first also take their bias through a bias tile: one 16 KB buffer per
+CTA, loaded by the producer after the K blocks of a layer's first unit in each step (bt_full on the
+leader, bt_empty per CTA), read by one bias MMA at the end of every unit of the layer, and released
+by a commit after the layer's last one.  The model checks that every bias MMA sees its own layer's
+tile and that no tile lands while a bias MMA of the previous one is pending.
+
 The decoder's unit walk is the kernel's one-launch schedule: each of six lanes runs a queue of
 pair-tiles back to back (longest first, to the least-loaded lane), cut into segments at every
 step where a lane changes tile, as `build_decode_schedule` in sc_mlp_tc.cu does for one pair.
@@ -131,6 +137,29 @@ def units(decode, n_tiles, maxlen):
                     yield grp, tt, g0 + tt, 0, L, nh
 
 
+def units_fl(decode, n_tiles, maxlen):
+    """units() with the kernel's fl flags: bit 0 the first unit of its (step or group, layer), bit 1
+    the last."""
+    us = list(units(decode, n_tiles, maxlen))
+    out = []
+    for i, u in enumerate(us):
+        key = (u[0], u[4])
+        first = i == 0 or (us[i - 1][0], us[i - 1][4]) != key
+        last = i == len(us) - 1 or (us[i + 1][0], us[i + 1][4]) != key
+        out.append(u + ((1 if first else 0) | (2 if last else 0),))
+    return out
+
+
+class Done:
+    """A commit entry that records the completion of an MMA (no barrier)."""
+
+    def __init__(self, fn):
+        self.fn = fn
+
+    def arrive(self):
+        self.fn()
+
+
 def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slots=False, abort=None):
     """Run one pair's roles to completion.  `plant` injects one protocol mistake into the model
     (tests of the model itself): 'counter' (a producer waits for one layer less), 'warp' (one
@@ -157,6 +186,13 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
     g_full = [Bar(f"g_full{b}", 4) for b in range(2)]
     g_empty = [[Bar(f"g_empty{b}/cta{r}", 1) for b in range(2)] for r in range(2)]
     drain = [Bar(f"drain/cta{r}", 1) for r in range(2)]
+    # decode (stage ring): the bias tile of layers >= 1, loaded once per step and layer into one
+    # buffer per CTA; bt_full on the leader (expect-tx + both CTAs' bytes), bt_empty per CTA (commit)
+    tiles = decode and not slots
+    bt_full = Bar("bt_full", 1)
+    bt_empty = [Bar(f"bt_empty/cta{r}", 1) for r in range(2)]
+    tile_in = [None, None]                          # per CTA: the (step, layer) whose tile has landed
+    tile_reads = {}                                 # (step, layer) -> bias MMAs issued, not completed
     act = [[0] * 8 for _ in range(2)]
     done = {}                        # (rank, gs, tt, L) -> epilogue warps finished with that layer
     tma, commits = [], []            # in flight: (bar, bytes) / lists of barriers to arrive on
@@ -190,8 +226,9 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
         uses = [0] * nbuf                             # per buffer: times filled so far
         led = [0] * nbuf                              # per buffer: K blocks it has led (full phases)
         issued = []                                   # per K block: (first buffer, its K block number, its fill number)
+        nbt = 0                                       # bias tiles loaded
         try:
-            for gs, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
+            for gs, tt, pt, step, L, nh, fl in units_fl(decode, n_tiles, maxlen):
                 if decode and nh == 1 and (L == 0 or not slots):
                     continue                          # loaded with half 0 (shared stages)
                 nkb = in_dim[L] // KB
@@ -227,6 +264,20 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
                     it += 1
                     pos += adv
                     yield
+                if tiles and L >= 1 and fl & 1:
+                    # the layer's bias tile, after the unit's K blocks, once the buffer is free
+                    yield from pwait(f"producer{rank}", bt_empty[rank], (nbt & 1) ^ 1, nbt)
+                    if rank == 0:
+                        bt_full.expect_tx(32)
+                        bt_full.arrive()
+
+                    def land(key=(gs, L), r=rank):
+                        for old_key, n in tile_reads.items():
+                            assert old_key == key or n == 0, "bias tile overwritten under a pending bias MMA"
+                        tile_in[r] = key
+                    tma.append((bt_full, 16, rank, land))
+                    nbt += 1
+                    yield
         except Timeout:
             if plant == "no_drain":
                 assert not [t for t in tma if t[2] == rank], \
@@ -241,6 +292,14 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
                         yield from parity_wait(empty[rank][s], u & 1, u + 1, 500)
                 except Timeout:
                     pass
+            if nbt:
+                try:
+                    if rank == 0:
+                        yield from parity_wait(bt_full, (nbt - 1) & 1, nbt, 500)
+                    else:
+                        yield from parity_wait(bt_empty[rank], (nbt - 1) & 1, nbt, 500)
+                except Timeout:
+                    pass
             yield from idle(400)
             # the producer is the only role that issues copies into this CTA's shared memory
             assert not [t for t in tma if t[2] == rank], "a CTA ends with copies still landing in its shared memory"
@@ -249,8 +308,9 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
         it = uu = li = pos = 0
         it_shared = 0                                 # first stage of the current shared layer
         firsts = [0] * nbuf                           # per buffer: K blocks it has led so far
+        nbt = 0                                       # bias tiles used
         try:
-            for gs, tt, pt, step, L, nh in units(decode, n_tiles, maxlen):
+            for gs, tt, pt, step, L, nh, fl in units_fl(decode, n_tiles, maxlen):
                 if decode and L == 0 and nh == 1:
                     continue
                 dual = decode and L == 0
@@ -286,6 +346,20 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
                     it += 1
                     pos += adv
                     yield
+                if tiles and L >= 1:
+                    # the bias MMA after the K blocks; the tile is released after the layer's last
+                    if fl & 1:
+                        yield from pwait("mma", bt_full, nbt & 1, nbt + 1)
+                        nbt += 1
+                    key = (gs, L)
+                    assert tile_in == [key, key], "bias MMA before its layer's tile landed"
+                    tile_reads[key] = tile_reads.get(key, 0) + 1
+
+                    def read_done(key=key):
+                        tile_reads[key] -= 1
+                    commits.append([Done(read_done)])
+                    if fl & (1 if plant == "tile" else 2):
+                        commits.append([bt_empty[0], bt_empty[1]])
                 commits.append([acc_full[0][ab], acc_full[1][ab]])
                 if dual:
                     commits.append([acc_full[0][ab ^ 1], acc_full[1][ab ^ 1]])
@@ -350,8 +424,10 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
     while live:
         choice = rng.random()
         if tma and choice < 0.15:
-            bar, b, _ = tma.pop(rng.randrange(len(tma)))
-            bar.complete_tx(b)
+            entry = tma.pop(rng.randrange(len(tma)))
+            if len(entry) > 3:
+                entry[3]()                            # the copy's data is in shared memory
+            entry[0].complete_tx(entry[1])
             stalled = 0
             continue
         if commits and choice < 0.3:
@@ -378,7 +454,7 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
     if abort:
         assert waits.get(abort[0], 0) >= abort[1], "the planted abort was never reached"
     if not abort:
-        for b in full + acc_empty + g_full:
+        for b in full + acc_empty + g_full + [bt_full]:
             assert b.pending == b.count and b.tx == 0, f"{b.name} left mid-phase"
 
 
@@ -416,6 +492,19 @@ def test_the_model_catches_planted_protocol_mistakes(plant, messages, slots):
             except AssertionError as e:
                 errors.append(str(e))
     assert errors and all(any(m in e for m in messages) for e in errors), errors[:3]
+
+
+def test_the_model_catches_an_early_bias_tile_release():
+    """Releasing the bias tile after a layer's first bias MMA instead of its last lets the next
+    layer's tile land while bias MMAs still read the buffer."""
+    errors = []
+    for seed in range(6):
+        for n_tiles, maxlen in [(4, [3, 3, 2, 1]), (12, [2] * 12)]:
+            try:
+                simulate(True, n_tiles, maxlen, seed=seed, plant="tile")
+            except AssertionError as e:
+                errors.append(str(e))
+    assert errors and all("bias" in e or "waiter targets phase" in e or "deadlock" in e for e in errors), errors[:3]
 
 
 @pytest.mark.parametrize("seed", range(2))
