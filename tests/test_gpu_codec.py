@@ -238,6 +238,27 @@ def test_random_model_streams_match_oracle(path):
     assert all(np.array_equal(a, b) for a, b in zip(back, chunks))
 
 
+def test_decoder_bias_outside_the_tile_range():
+    """The pair decoder adds the bias of layers after the first with an MMA against a bias tile of
+    int8 digits, which reaches |b| <= 258,127; a layer with a bias beyond that keeps its bias in the
+    epilogue.  A model mixing both kinds of layer must still decode the oracle's streams."""
+    from sigcomp_b200.model import random_model
+    model = random_model(7)
+    for layer in (2, len(model.biases) - 1):
+        b = np.asarray(model.biases[layer]).copy()
+        b[::37] = np.where(b[::37] >= 0, 300_000, -300_000)
+        model.biases[layer] = b
+    rng = np.random.default_rng(7)
+    chunks = [rng.integers(0, 256, size=n).astype(np.uint8) for n in (1, 300, 2048, 1500, 64)]
+    om = OracleModel(model)
+    streams = om.compress_chunks(chunks)
+    for path in ALL_PATHS:
+        codec = _codec(model, path)
+        assert codec.compress_chunks(chunks) == streams, path
+        back = codec.decompress_chunks(streams, [len(c) for c in chunks])
+        assert all(np.array_equal(a, c) for a, c in zip(back, chunks)), path
+
+
 def test_synthetic_reads_match_oracle(lossless_model):
     from oracle import signal
     from sigcomp_b200 import synthetic
