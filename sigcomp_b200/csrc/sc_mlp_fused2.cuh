@@ -52,7 +52,7 @@ struct Fused2Params {
     // of CTA r's tile serves output column h * 256 + r * 128 + i of half h: bytes 64h .. 64h + 31
     // hold 32 int8 digits of that column's bias and bytes 64h + 32 .. 64h + 63 the constants
     // 16 x 127, 16 x 1.  One K = 32 MMA with the constants as A (the same in every row) and the
-    // digits as B puts the bias into the accumulator before the layer's K blocks.
+    // digits as B adds the bias to the accumulator after a unit's K blocks.
     CUtensorMap bt[FMAX_LAYERS];
     uint32_t bias_mma;                // bit L: layer L's bias enters through its bias tile
     CUtensorMap act[2];               // activation ping-pong, box 128 x 128 B
