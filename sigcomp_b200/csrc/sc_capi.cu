@@ -232,7 +232,7 @@ int sc_model_create(int device, int32_t window, int32_t emb_dim, int32_t num_lay
             SC_CUDA(cudaMemcpy(L.w, weights[l], wb, cudaMemcpyHostToDevice));
             SC_CUDA(cudaMalloc(&L.bias, sizeof(int32_t) * L.out_dim));
             SC_CUDA(cudaMemcpy(L.bias, biases[l], sizeof(int32_t) * L.out_dim, cudaMemcpyHostToDevice));
-            // the pair decoder adds the bias of layers >= 1 with an MMA (fast requantisation only)
+            // the pair kernels add the bias of layers >= 1 with an MMA (fast requantisation only)
             const std::vector<int8_t> bt = l > 0 && L.rq.hi_path ? bias_tile(biases[l], L.out_dim)
                                                                    : std::vector<int8_t>();
             if (!bt.empty()) {

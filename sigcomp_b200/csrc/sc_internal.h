@@ -134,7 +134,7 @@ struct LayerDev {
     int8_t *w = nullptr;        // [out][in] row-major (CUDA-core path)
     int8_t *w_tc = nullptr;     // tensor-core operand layout (tcgen05 path), or null
     int32_t *bias = nullptr;    // [out]
-    // bias tile of the pair decoder, [256][128] int8 (null when the bias stays in the epilogue):
+    // bias tile of the pair kernels, [256][128] int8 (null when the bias stays in the epilogue):
     // row n holds, for each 256-column half h, 32 int8 digits of bias[h * 256 + n] in bytes
     // 64h .. 64h + 31 and the multipliers 16 x 127, 16 x 1 in bytes 64h + 32 .. 64h + 63
     int8_t *bdig = nullptr;

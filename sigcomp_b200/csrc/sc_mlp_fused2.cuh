@@ -21,9 +21,9 @@
 //     one 128-row x 128-byte block per window position); the last-layer
 //     epilogue appends each decoded token's embedding row, so a step writes
 //     one block per tile instead of building all 64.
-//   - decode: the layers after the first add their bias with one K = 32 MMA
-//     against a resident bias tile (loaded once per layer and step), so their
-//     epilogues requantise without loading or adding a bias.
+//   - the layers after the first add their bias with one K = 32 MMA against
+//     a resident bias tile (loaded once per layer and step or tile group), so
+//     their epilogues requantise without loading or adding a bias.
 // No TMA load uses cluster multicast.
 #pragma once
 
@@ -48,7 +48,7 @@ struct DecSeg {
 
 struct Fused2Params {
     CUtensorMap w[FMAX_LAYERS];       // weights, box 128 rows x 128 B (half of a 256-row unit)
-    // decode: bias tiles of layers >= 1 (box 128 rows x 128 B, one per CTA of the pair).  Row i
+    // bias tiles of layers >= 1 (box 128 rows x 128 B, one per CTA of the pair).  Row i
     // of CTA r's tile serves output column h * 256 + r * 128 + i of half h: bytes 64h .. 64h + 31
     // hold 32 int8 digits of that column's bias and bytes 64h + 32 .. 64h + 63 the constants
     // 16 x 127, 16 x 1.  One K = 32 MMA with the constants as A (the same in every row) and the
@@ -114,9 +114,9 @@ struct F2Cfg {
     static constexpr int STAGE_BYTES = A_BYTES + (DECODE ? 2 : 1) * B_HALF;   // 48 KB / 32 KB
     static constexpr int OFF_X = STAGES * STAGE_BYTES;                    // 192 KB / 128 KB
     static constexpr int X_BYTES = DECODE ? 0 : 2 * G_BYTES;
-    // decode: the current layer's bias tile (16 KB); its SMEM bias table holds layer 0 only
+    // the current layer's bias tile (16 KB); the decoder's SMEM bias table holds layer 0 only
     static constexpr int OFF_BT = OFF_X + X_BYTES;
-    static constexpr int BT_BYTES = DECODE ? TM * KB : 0;
+    static constexpr int BT_BYTES = TM * KB;
     static constexpr int OFF_BIAS = OFF_BT + BT_BYTES;
     static constexpr int BIAS_ENTRIES = DECODE ? MAX_N : BIAS_MAX;
     static constexpr int OFF_LUT = OFF_BIAS + BIAS_ENTRIES * 4;
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
     uint64_t *g_full = acc_empty + 2, *g_empty = g_full + 2;
     // drain: the MMA issuer's last commit (both CTAs); TMEM is freed only after it
     uint64_t *drain = g_empty + 2;
-    // decode: bias tile loaded (leader: expect-tx + both CTAs' bytes) / free again (MMA commit)
+    // bias tile loaded (leader: expect-tx + both CTAs' bytes) / free again (MMA commit)
     uint64_t *bt_full = drain + 1, *bt_empty = drain + 2;
     uint8_t *btile = smem + C::OFF_BT;
     // act_cnt[tt]: +1 per epilogue warp of this CTA when its tile of slot tt finishes a
@@ -458,8 +458,8 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     }
                     tma_load_2d_pair(st + A_BYTES, &p.w[L], fb, kb * KB, nh * TN + (int)rank * (TN / 2));
                 }
-                if (DECODE && L != 0 && (fl & 1) && ((p.bias_mma >> L) & 1u)) {
-                    // the layer's bias tile, once per layer and step, after the first unit's K
+                if (L != 0 && (fl & 1) && ((p.bias_mma >> L) & 1u)) {
+                    // the layer's bias tile, once per layer and step (or group), after the first unit's K
                     // blocks and once the previous layer's last bias MMA has read the buffer
                     if (!mbar_wait_cluster(bt_empty, (nbt & 1) ^ 1)) return !(aborted = true);
                     if (rank == 0) mbar_arrive_expect_tx(bt_full, 2 * C::BT_BYTES);
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                     else mbar_wait_cluster_drain(&empty[s], ph);
                 }
                 // the last bias tile, the same way
-                if (DECODE && nbt > 0) {
+                if (nbt > 0) {
                     if (rank == 0) mbar_wait_cluster_drain(bt_full, (nbt - 1) & 1);
                     else mbar_wait_cluster_drain(bt_empty, (nbt - 1) & 1);
                 }
@@ -516,10 +516,10 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
                 tc_fence_after();
                 const uint32_t d = tmem_base + ab * TN;
                 const int kstep = (!DECODE && L == 0) ? 2 : 1;
-                // decode, bias tile: after the K blocks one K = 32 MMA adds the bias to the
-                // accumulator (integer sums: the order does not matter), so the tile has the
-                // unit's K blocks to arrive; it is released after the layer's last bias MMA
-                const bool bmma = DECODE && L != 0 && ((p.bias_mma >> L) & 1u);
+                // bias tile: after the K blocks one K = 32 MMA adds the bias to the accumulator
+                // (integer sums: the order does not matter), so the tile has the unit's K blocks
+                // to arrive; it is released after the layer's last bias MMA
+                const bool bmma = L != 0 && ((p.bias_mma >> L) & 1u);
                 if (shared0) it_shared = it;
                 if (shared1) {
                     for (int kb = 0; kb < nkb; ++kb) {
@@ -630,13 +630,14 @@ __global__ void __launch_bounds__(FUSED2_THREADS, 1) k_fused2(const __grid_const
             const bool rq_fast = rq.hi_path != 0;
             const int32_t rq_m0 = (int32_t)rq.m0, rq_hs = rq.hi_shift, rq_one = rq.one;
             const uint32_t rq_relu = rq.lo == 0 ? 0xFFFFFFFFu : 0u;
-            // decode keeps only layer 0's bias in SMEM; the other layers' biases enter through
-            // their bias tiles (nb), or are read from global memory when a layer has none
+            // the layers after the first take their bias through their bias tiles (nb); without a
+            // tile, compress reads it from SMEM and the decoder (which keeps only layer 0's bias
+            // in SMEM) from global memory
             const int32_t *bias = (!DECODE || L == 0) ? bias_s + L * MAX_N : p.bias[L];
-            const bool nb = DECODE && L != 0 && ((p.bias_mma >> L) & 1u);
+            const bool nb = L != 0 && ((p.bias_mma >> L) & 1u);
             const uint32_t acc_empty_leader = map_to_rank(&acc_empty[ab], 0);
             const int tile = 2 * pt + (int)rank;
-            // hidden layers; NB: the accumulator holds the bias already (decode, bias tile).  The
+            // hidden layers; NB: the accumulator holds the bias already (bias tile).  The
             // two forms are separate instantiations, so neither carries the other's registers.
             auto hidden_unit = [&](auto NB) -> bool {
                 int8_t *dst_row = p.act_ptr[L & 1] + (size_t)(slot_row0 + tt * TM + r) * MAX_N + nh * TN;

@@ -20,8 +20,8 @@ stages: the producer loads a K block's activations and both weight halves once (
 MMA issuer's half 0 waits for each stage and keeps it, and half 1 reads the same stages again and
 releases them.
 
-The decoder's layers after the first also take their bias through a bias tile: one 16 KB buffer per
-CTA, loaded by the producer after the K blocks of a layer's first unit in each step (bt_full on the
+Both kernels' layers after the first also take their bias through a bias tile: one 16 KB buffer per
+CTA, loaded by the producer after the K blocks of a layer's first unit in each step or tile group (bt_full on the
 leader, bt_empty per CTA), read by one bias MMA at the end of every unit of the layer, and released
 by a commit after the layer's last one.  The model checks that every bias MMA sees its own layer's
 tile and that no tile lands while a bias MMA of the previous one is pending.
@@ -186,9 +186,9 @@ def simulate(decode, n_tiles, maxlen=None, l0_kblocks=8, seed=0, plant=None, slo
     g_full = [Bar(f"g_full{b}", 4) for b in range(2)]
     g_empty = [[Bar(f"g_empty{b}/cta{r}", 1) for b in range(2)] for r in range(2)]
     drain = [Bar(f"drain/cta{r}", 1) for r in range(2)]
-    # decode (stage ring): the bias tile of layers >= 1, loaded once per step and layer into one
-    # buffer per CTA; bt_full on the leader (expect-tx + both CTAs' bytes), bt_empty per CTA (commit)
-    tiles = decode and not slots
+    # stage ring: the bias tile of layers >= 1, loaded once per step (or tile group) and layer into
+    # one buffer per CTA; bt_full on the leader (expect-tx + both CTAs' bytes), bt_empty per CTA (commit)
+    tiles = not slots
     bt_full = Bar("bt_full", 1)
     bt_empty = [Bar(f"bt_empty/cta{r}", 1) for r in range(2)]
     tile_in = [None, None]                          # per CTA: the (step, layer) whose tile has landed
